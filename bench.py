@@ -1,0 +1,336 @@
+"""Benchmark of the batched token sampler (franzvill/quasar sample.c rebuilt for B200).
+
+Workload (the headline): per GPU, B=4096 rows of
+V=151936 fp32 logits ~N(0,3) (synthetic, seeded), per-row temperature
+U[0.2,1.5], top_k off, top_p 0.95, min_p 0.05, repeat_penalty 1.1 over a
+256-id history ring per row, row-indexed PRNG seeds, record on.
+One step = one quasar_sampler_pick_batch call over the B rows. Rows are
+independent, so N GPUs run N shards with no collective ("scaling": "weak").
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line on rank 0. `value` is device-timed (CUDA events, inputs
+resident in HBM, 2.49 GB per step > L2); `e2e` times the same call through the
+public API with the logits copied from pinned host memory every step and the
+ids read back. `--impl reference` times the reference sample.c (compiled
+unmodified into oracle/_ref) on the host cores on bounded row samples.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+V = 151936
+B = 4096
+H = 256
+SEED_LOGITS, SEED_HIST, SEED_TEMP, SEED_RNG = 3, 33, 3, 5000
+METRIC = "sampled rows/s at V=151936, B=4096; % HBM roofline at 1/2/4/8 B200"
+# algorithmic bytes per row: logits V*4 + history H*4 + ring len/head 8 + params 24
+# + rng read/write 16 + id 4 + ring append 8
+BYTES_PER_ROW = V * 4 + H * 4 + 60
+FALLBACK_HBM_GBS = 6650.0
+
+
+def workload_config(n_gpus: int) -> dict:
+    return {"workload": "config3: N(0,3) logits, per-row T~U[0.2,1.5], top_p 0.95, min_p 0.05, "
+                        "repeat_penalty 1.1 over 256 history ids, record on",
+            "rows_per_gpu": B, "vocab": V, "history": H, "global_batch": B * n_gpus,
+            "parallelism": f"rows x{n_gpus}",
+            "l2": "inputs larger than L2 (2.49 GB of logits per step per GPU)"}
+
+
+def peak_hbm() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic_per_launch() -> float | None:
+    """DRAM bytes per launch of the sampler kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "sample_rows_config3_traffic.txt")
+    try:
+        with open(p) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_launch_full_size="):
+                    return float(line.split("=", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled while GPU work runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus: str):
+        self.gpus = gpus
+        self.rows: list[list[str]] = []
+        self.proc = None
+        self.th = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.gpus, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return self
+        self.th = threading.Thread(target=self._read, daemon=True)
+        self.th.start()
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def stop(self) -> dict | None:
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.th:
+            self.th.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_rows(n_rows: int, row0: int = 0):
+    """Config-3 rows [row0, row0+n_rows) generated on the CPU (same bits as the GPU)."""
+    from oracle import oracle as O
+    logits = O.synth_logits(O.SYNTH_NORMAL, SEED_LOGITS, row0, n_rows, V, 3.0)
+    hist = O.synth_hist(SEED_HIST, row0, n_rows, H, V)
+    temps = O.synth_uniform(SEED_TEMP, row0, n_rows, 0.2, 1.5)
+    prm = O.make_params(n_rows, temperature=temps, top_p=0.95, min_p=0.05, repeat_penalty=1.1)
+    seeds = np.arange(row0, row0 + n_rows, dtype=np.uint64) + np.uint64(SEED_RNG)
+    return logits, hist, prm, seeds
+
+
+def time_cpu_reference(n_rows: int, threads: int, row0: int = 0):
+    """(rows/s, backend kind) of the reference sampler on host cores."""
+    from oracle import oracle as O
+    backend = O.best_backend()
+    logits, hist, prm, seeds = cpu_rows(n_rows, row0)
+    t0 = time.perf_counter()
+    O.pick_rows(logits, prm, seeds, hist=hist, backend=backend, nthreads=threads)
+    dt = time.perf_counter() - t0
+    return n_rows / dt, ("reference" if backend == "ref" else "port"), dt
+
+
+def run_reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    if not O.available("ref") and not O.available("oracle"):
+        O.build()
+    threads = cpu_threads()
+    sample = 8 * threads
+    backend = O.best_backend()
+    for w in range(args.warmup):
+        time_cpu_reference(min(sample, 2 * threads), threads, row0=w * sample)
+    rates, total_rows, total_t = [], 0, 0.0
+    for k in range(args.steps):
+        logits, hist, prm, seeds = cpu_rows(sample, row0=k * sample)
+        t0 = time.perf_counter()
+        O.pick_rows(logits, prm, seeds, hist=hist, backend=backend, nthreads=threads)
+        dt = time.perf_counter() - t0
+        rates.append(sample / dt)
+        total_rows += sample
+        total_t += dt
+    value = total_rows / total_t
+    kind = "reference" if backend == "ref" else "port"
+    line = {"metric": METRIC, "value": value, "unit": "rows/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * total_t / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args.gpus),
+            "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": kind,
+                             "sample": f"{sample} config-3 rows per step (rows [k*{sample}, "
+                                       f"(k+1)*{sample}) of the workload), one sampler object "
+                                       f"per row, {threads} pthreads"},
+            "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    import quasar_b200 as q
+
+    row0 = rank * B  # each rank samples its own rows of the synthetic batch
+    logits = torch.empty(B, V, dtype=torch.float32, device=dev)
+    q.synth_logits(q.SYNTH_NORMAL, SEED_LOGITS, row0, B, V, 3.0, logits)
+    hist = torch.empty(B, H, dtype=torch.int32, device=dev)
+    q.synth_hist(SEED_HIST, row0, B, H, V, hist)
+    temps = torch.empty(B, dtype=torch.float32, device=dev)
+    q.synth_uniform(SEED_TEMP, row0, B, 0.2, 1.5, temps)
+    prm = q.make_params(B, temperature=temps.cpu().numpy(), top_p=0.95, min_p=0.05,
+                        repeat_penalty=1.1)
+    d_params = q.params_to_device(prm, dev)
+    seeds = np.arange(row0, row0 + B, dtype=np.uint64) + np.uint64(SEED_RNG)
+    rng = torch.from_numpy(seeds.view(np.int64).copy()).to(dev)
+    hist_len = torch.full((B,), H, dtype=torch.int32, device=dev)
+    hist_head = torch.zeros(B, dtype=torch.int32, device=dev)
+    out = torch.empty(B, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(src=logits):
+        q.pick_batch(src, rng, d_params=d_params, hist=hist, hist_len=hist_len,
+                     hist_head=hist_head, record=True, out=out, stream=stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+
+    clocks = ClockSampler(",".join(str(i) for i in range(world)) if world > 1 else str(local))
+    if rank == 0:
+        clocks.start()
+        time.sleep(0.2)
+    # ---- device-timed region: inputs resident in HBM ----
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+
+    # ---- end to end through the public API, host buffers ----
+    e2e_steps = max(1, min(args.steps, 5))
+    host = torch.empty(B, V, dtype=torch.float32, pin_memory=True)
+    host.copy_(logits)
+    ids_host = torch.empty(B, dtype=torch.int32, pin_memory=True)
+    stage = torch.empty_like(logits)
+    h2d = B * V * 4
+    d2h = B * 4
+    barrier()
+    torch.cuda.synchronize(dev)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(e2e_steps):
+        stage.copy_(host, non_blocking=True)
+        step(stage)
+        ids_host.copy_(out, non_blocking=True)
+    f1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    t2 = torch.tensor([f0.elapsed_time(f1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t2.item())
+    clk = clocks.stop() if rank == 0 else None
+
+    rows_total = B * world * args.steps
+    value = rows_total / (ms_max / 1e3)
+    per_launch_s = (ms / 1e3) / args.steps  # one kernel launch per step
+    achieved = B * BYTES_PER_ROW / per_launch_s / 1e9
+    peak, peak_kind = peak_hbm()
+    traffic = ncu_traffic_per_launch()
+    line = {"metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": workload_config(world),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": peak_kind,
+                         "algorithmic_bytes_per_launch": B * BYTES_PER_ROW},
+            "e2e": {"value": B * world * e2e_steps / (e2e_ms / 1e3), "unit": "rows/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps * q.lib().quasar_sampler_pick_batch_launches(),
+            "clocks": clk}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = cpu_threads()
+        rows = max(64, min(1024, 32 * threads))
+        rate, kind, dt = time_cpu_reference(rows, threads)
+        line["cpu_baseline"] = {"value": rate, "unit": "rows/s", "cores": threads, "kind": kind,
+                                "sample": f"first {rows} rows of the config-3 workload "
+                                          f"({dt:.1f} s wall on {threads} threads)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

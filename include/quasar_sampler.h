@@ -1,0 +1,155 @@
+/* quasar_sampler.h - C ABI of libquasar_cuda, the B200 token sampler.
+ *
+ * A drop-in for franzvill/quasar's sampler (sample.h / sample.c): the five
+ * sample.h entry points keep their names, signatures and meaning, and a batched
+ * entry point samples B rows of device-resident logits per call on sm_100a.
+ * All pointers named d_* are device pointers; `stream` is a cudaStream_t
+ * (NULL = the legacy default stream). Status codes are QUASAR_OK (0) or one of
+ * the negative QUASAR_E* values; nothing aborts and nothing falls back to the
+ * CPU.
+ *
+ * Sampling semantics are those of sample.c:111-178, row by row:
+ *   repeat penalty over the row's history ring (ids marked once, l>0 ? l/rp : l*rp)
+ *   -> temperature <= 0: argmax, first index on ties, no PRNG draw
+ *   -> inv_t = 1.0f/T, window sc >= max*inv_t - 30, softmax (double sum)
+ *   -> order by p descending, ties by id ascending
+ *   -> top-k, top-p (double cumsum >= top_p), min-p (p < min_p * p_max cuts)
+ *   -> one xorshift64* draw u in [0,1), first kept index with u*rsum <= cumsum
+ *   -> optional append of the chosen id to the history ring. */
+#ifndef QUASAR_SAMPLER_H
+#define QUASAR_SAMPLER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QUASAR_OK               0
+#define QUASAR_EINVAL          -1  /* bad argument (size, pointer, alignment) */
+#define QUASAR_EUNSUPPORTED    -2  /* shape outside what the kernels support */
+#define QUASAR_ECUDA           -3  /* a CUDA runtime call failed */
+#define QUASAR_ENOMEM          -4  /* device or host allocation failed */
+#define QUASAR_ENCCL           -5  /* an NCCL call failed or timed out */
+#define QUASAR_EOVERFLOW       -6  /* a fixed-capacity buffer was too small */
+
+/* ---- sample.h drop-in --------------------------------------------------- */
+
+typedef struct quasar_sampler quasar_sampler;
+
+/* Replaces sample.h:14 / sample.c:31-39. Defaults: greedy (temperature 0),
+ * top_p 1, top_k 0, min_p 0, repeat_penalty 1, repeat_last_n 0, PRNG state
+ * 0x9E3779B97F4A7C15. Device buffers are allocated lazily on the current CUDA
+ * device. Returns NULL when the host allocation fails. */
+quasar_sampler *quasar_sampler_new(void);
+
+/* Replaces sample.h:15 / sample.c:41-45. NULL-safe. */
+void quasar_sampler_free(quasar_sampler *s);
+
+/* Replaces sample.h:19-22 / sample.c:47-68, same clamps: top_p outside (0,1)
+ * -> 1, top_k <= 0 -> 0, min_p <= 0 -> 0, repeat_penalty <= 1 -> 1,
+ * repeat_last_n <= 0 -> 0; seed 0 -> time-seeded; history cleared. */
+void quasar_sampler_config(quasar_sampler *s,
+                           float temperature, float top_p, int top_k,
+                           float min_p, float repeat_penalty, int repeat_last_n,
+                           uint64_t seed);
+
+/* Replaces sample.h:25 / sample.c:70: clears history, keeps the PRNG state. */
+void quasar_sampler_reset(quasar_sampler *s);
+
+/* Replaces sample.h:29 / sample.c:111-178. logits[n_vocab] may be a host
+ * pointer (copied to the device) or a device pointer (read in place); it is
+ * not modified. Records the choice in history. n_vocab <= 0 returns 0, as in
+ * the reference. On a CUDA failure returns -1 and quasar_sampler_last_error()
+ * gives the status (the reference has no error path here; -1 is never a valid
+ * token id). Blocks until the id is on the host. */
+int quasar_sampler_pick(quasar_sampler *s, const float *logits, int n_vocab);
+
+/* Extension: status of the last call on s (QUASAR_OK or QUASAR_E*). */
+int quasar_sampler_last_error(const quasar_sampler *s);
+
+/* Extension: human-readable name of a status code. */
+const char *quasar_status_string(int status);
+
+/* ---- batched sampler ------------------------------------------------------ */
+
+/* Per-row parameters, raw (clamped inside, as quasar_sampler_config does). */
+typedef struct {
+    float   temperature;
+    float   top_p;
+    float   min_p;
+    float   repeat_penalty;
+    int32_t top_k;
+    int32_t reserved;        /* set to 0 */
+} quasar_sample_params;
+
+/* Optional per-row report. */
+typedef struct {
+    int32_t n_kept;          /* survivors of top-k/top-p/min-p (0 when greedy) */
+    float   p_chosen;        /* normalised probability of the chosen id (greedy: 1) */
+    float   inv_sum;         /* (float)(1 / window sum) (greedy: 0) */
+    int32_t path;            /* QUASAR_PATH_* that produced the row */
+} quasar_pick_diag;
+
+#define QUASAR_PATH_GREEDY     0   /* temperature <= 0: penalized argmax */
+#define QUASAR_PATH_CANDIDATE  1   /* candidates collected in one HBM pass, exact cuts */
+#define QUASAR_PATH_SELECT     2   /* exact radix select over the row (any params) */
+
+/* Flags for quasar_sampler_pick_batch. */
+#define QUASAR_FLAG_EXACT_SELECT  1  /* route every stochastic row through the
+                                        radix-select path (same results; slower) */
+
+/* Sample B rows of d_logits (row r at d_logits + r*ld, V columns, fp32).
+ *   d_params    [B] per-row parameters on the device, or NULL to use *h_params
+ *               for every row (h_params must then be non-NULL).
+ *   d_rng       [B] xorshift64* states, advanced in place: one step per
+ *               stochastic row, none for a greedy row (sample.c:72-81, 130-134).
+ *   d_hist      [B, hist_cap] history rings (sample.c:22-23); row r holds
+ *               d_hist_len[r] ids starting at d_hist_head[r]. hist_cap == 0
+ *               disables history (d_hist may then be NULL). d_hist_len NULL
+ *               means every ring is full; d_hist_head NULL means head 0.
+ *   record      nonzero: append each chosen id to its ring the way sample.c:83-92
+ *               does (needs d_hist_len and d_hist_head).
+ *   d_out       [B] chosen ids.
+ *   d_diag      [B] optional report, or NULL.
+ * Requirements: 1 <= V <= QUASAR_MAX_VOCAB, ld >= V. Rows whose start is
+ * 16-byte aligned with ld % 4 == 0 take the vectorised loads. Finite logits
+ * only (as in the reference, NaN/inf give unspecified picks). Asynchronous on
+ * `stream`; returns after the launch. Replaces, batched, sample.h:29. */
+#define QUASAR_MAX_VOCAB (1 << 20)
+int quasar_sampler_pick_batch(const float *d_logits, int64_t ld, int B, int V,
+                              const quasar_sample_params *d_params,
+                              const quasar_sample_params *h_params,
+                              uint64_t *d_rng,
+                              int32_t *d_hist, int hist_cap,
+                              int32_t *d_hist_len, int32_t *d_hist_head,
+                              int record,
+                              int32_t *d_out, quasar_pick_diag *d_diag,
+                              int flags, void *stream);
+
+/* Number of kernel launches one quasar_sampler_pick_batch call makes (1). */
+int quasar_sampler_pick_batch_launches(void);
+
+/* ---- synthetic inputs (benchmark / test utility, not in the reference) ---- */
+
+#define QUASAR_SYNTH_NORMAL       0  /* Irwin-Hall N(0,1) * scale */
+#define QUASAR_SYNTH_GUMBEL_PEAK  1  /* Gumbel(0,1), +8 at one column per row */
+#define QUASAR_SYNTH_ZIPF         2  /* -scale * log(rank), rank a row permutation */
+
+/* Fill rows [row0, row0+B) of a deterministic synthetic logits matrix into
+ * d_out (row stride ld). Bit-identical to the CPU recipe used by the tests. */
+int quasar_synth_logits(int kind, uint64_t seed, int64_t row0, int B, int V,
+                        int64_t ld, float scale, float *d_out, void *stream);
+/* History ids uniform in [0, V): d_out[B, H]. */
+int quasar_synth_hist(uint64_t seed, int64_t row0, int B, int H, int V,
+                      int32_t *d_out, void *stream);
+/* Per-row uniform values lo + (hi-lo)*u24: d_out[B]. */
+int quasar_synth_uniform(uint64_t seed, int64_t row0, int B, float lo, float hi,
+                         float *d_out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QUASAR_SAMPLER_H */

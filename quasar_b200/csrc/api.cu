@@ -1,0 +1,254 @@
+// api.cu - C ABI of libquasar_cuda: the sample.h drop-in and the batched entry.
+//
+// Reference interface replaced: franzvill/quasar sample.h:12-29 (sample.c:31-178).
+// The sampler object keeps the reference's host-side fields (params, clamps,
+// seeding) and moves the state that a pick touches - the PRNG word and the
+// history ring - into device memory, so a pick is one kernel launch.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
+
+#include "../../include/quasar_sampler.h"
+#include "sample_rows.cuh"
+
+struct quasar_sampler {
+    // configuration after the clamps of sample.c:51-56
+    float temperature, top_p, min_p, repeat_penalty;
+    int top_k, repeat_last_n;
+    uint64_t seed_state;  // PRNG word to upload when `rng_dirty`
+    int rng_dirty;
+
+    // device state, allocated lazily on `device`
+    int device;
+    cudaStream_t stream;
+    uint64_t* d_rng;
+    int32_t* d_meta;  // [0] ring length, [1] ring head, [2] chosen id
+    int32_t* d_hist;
+    int hist_cap;
+    float* d_logits;
+    int logits_cap;
+    int32_t* h_id;  // pinned
+    int last_error;
+};
+
+namespace {
+
+int set_err(quasar_sampler* s, int rc) {
+    if (s) s->last_error = rc;
+    return rc;
+}
+
+int ensure_device(quasar_sampler* s) {
+    if (s->stream) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess) return QUASAR_ECUDA;
+        if (dev != s->device && cudaSetDevice(s->device) != cudaSuccess) return QUASAR_ECUDA;
+        return QUASAR_OK;
+    }
+    if (cudaGetDevice(&s->device) != cudaSuccess) return QUASAR_ECUDA;
+    if (cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        s->stream = nullptr;
+        return QUASAR_ECUDA;
+    }
+    if (cudaMalloc(&s->d_rng, sizeof(uint64_t)) != cudaSuccess) return QUASAR_ENOMEM;
+    if (cudaMalloc(&s->d_meta, 4 * sizeof(int32_t)) != cudaSuccess) return QUASAR_ENOMEM;
+    if (cudaMallocHost(&s->h_id, sizeof(int32_t)) != cudaSuccess) return QUASAR_ENOMEM;
+    if (cudaMemsetAsync(s->d_meta, 0, 4 * sizeof(int32_t), s->stream) != cudaSuccess)
+        return QUASAR_ECUDA;
+    s->rng_dirty = 1;
+    return QUASAR_OK;
+}
+
+int sync_config(quasar_sampler* s) {
+    int rc = ensure_device(s);
+    if (rc != QUASAR_OK) return rc;
+    // sample.c:61-66: the ring is reallocated only for a new nonzero capacity;
+    // repeat_last_n = 0 keeps an existing ring (and its recording) in place.
+    if (s->repeat_last_n > 0 && s->repeat_last_n != s->hist_cap) {
+        if (s->d_hist) cudaFree(s->d_hist);
+        s->d_hist = nullptr;
+        s->hist_cap = 0;
+        if (cudaMalloc(&s->d_hist, (size_t)s->repeat_last_n * sizeof(int32_t)) != cudaSuccess)
+            return QUASAR_ENOMEM;
+        if (cudaMemsetAsync(s->d_hist, 0, (size_t)s->repeat_last_n * sizeof(int32_t),
+                            s->stream) != cudaSuccess)
+            return QUASAR_ECUDA;
+        s->hist_cap = s->repeat_last_n;
+    }
+    if (s->rng_dirty) {
+        if (cudaMemcpyAsync(s->d_rng, &s->seed_state, sizeof(uint64_t), cudaMemcpyHostToDevice,
+                            s->stream) != cudaSuccess)
+            return QUASAR_ECUDA;
+        // the host word must outlive the async copy
+        if (cudaStreamSynchronize(s->stream) != cudaSuccess) return QUASAR_ECUDA;
+        s->rng_dirty = 0;
+    }
+    return QUASAR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* quasar_status_string(int status) {
+    switch (status) {
+        case QUASAR_OK: return "ok";
+        case QUASAR_EINVAL: return "invalid argument";
+        case QUASAR_EUNSUPPORTED: return "unsupported shape";
+        case QUASAR_ECUDA: return "CUDA error";
+        case QUASAR_ENOMEM: return "out of memory";
+        case QUASAR_ENCCL: return "NCCL error";
+        case QUASAR_EOVERFLOW: return "buffer overflow";
+        default: return "unknown status";
+    }
+}
+
+int quasar_sampler_pick_batch_launches(void) { return 1; }
+
+int quasar_sampler_pick_batch(const float* d_logits, int64_t ld, int B, int V,
+                              const quasar_sample_params* d_params,
+                              const quasar_sample_params* h_params, uint64_t* d_rng,
+                              int32_t* d_hist, int hist_cap, int32_t* d_hist_len,
+                              int32_t* d_hist_head, int record, int32_t* d_out,
+                              quasar_pick_diag* d_diag, int flags, void* stream) {
+    if (B < 0 || V < 1 || V > QUASAR_MAX_VOCAB || ld < V) return QUASAR_EINVAL;
+    if (B == 0) return QUASAR_OK;
+    if (!d_logits || !d_rng || !d_out || (!d_params && !h_params)) return QUASAR_EINVAL;
+    if (hist_cap < 0 || (hist_cap > 0 && !d_hist)) return QUASAR_EINVAL;
+    if (record && hist_cap > 0 && (!d_hist_len || !d_hist_head)) return QUASAR_EINVAL;
+    if (qs::rows_smem_bytes(V) > 220 * 1024) return QUASAR_EUNSUPPORTED;
+    qs::RowsArgs a;
+    memset(&a, 0, sizeof a);
+    a.logits = d_logits;
+    a.ld = ld;
+    a.B = B;
+    a.V = V;
+    a.d_params = d_params;
+    if (h_params) a.h_params = *h_params;
+    a.rng = d_rng;
+    a.hist = hist_cap > 0 ? d_hist : nullptr;
+    a.hist_cap = hist_cap;
+    a.hist_len = d_hist_len;
+    a.hist_head = d_hist_head;
+    a.record = record;
+    a.out = d_out;
+    a.diag = d_diag;
+    a.flags = flags;
+    a.vec = ((uintptr_t)d_logits % 16 == 0) && (ld % 4 == 0);
+    const cudaError_t err = qs::launch_sample_rows(a, B, (cudaStream_t)stream);
+    return err == cudaSuccess ? QUASAR_OK : QUASAR_ECUDA;
+}
+
+quasar_sampler* quasar_sampler_new(void) {
+    quasar_sampler* s = (quasar_sampler*)calloc(1, sizeof *s);
+    if (!s) return nullptr;
+    s->temperature = 0.0f;  // greedy by default (sample.c:34)
+    s->top_p = 1.0f;
+    s->top_k = 0;
+    s->min_p = 0.0f;
+    s->repeat_penalty = 1.0f;
+    s->repeat_last_n = 0;
+    s->seed_state = 0x9E3779B97F4A7C15ull;  // sample.c:37
+    s->rng_dirty = 1;
+    return s;
+}
+
+void quasar_sampler_free(quasar_sampler* s) {
+    if (!s) return;
+    if (s->stream) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev != s->device) cudaSetDevice(s->device);
+        cudaStreamSynchronize(s->stream);
+        cudaFree(s->d_rng);
+        cudaFree(s->d_meta);
+        cudaFree(s->d_hist);
+        cudaFree(s->d_logits);
+        cudaFreeHost(s->h_id);
+        cudaStreamDestroy(s->stream);
+        if (dev != s->device) cudaSetDevice(dev);
+    }
+    free(s);
+}
+
+void quasar_sampler_config(quasar_sampler* s, float temperature, float top_p, int top_k,
+                           float min_p, float repeat_penalty, int repeat_last_n, uint64_t seed) {
+    if (!s) return;
+    s->temperature = temperature;
+    s->top_p = (top_p > 0.0f && top_p < 1.0f) ? top_p : 1.0f;
+    s->top_k = top_k > 0 ? top_k : 0;
+    s->min_p = min_p > 0.0f ? min_p : 0.0f;
+    s->repeat_penalty = repeat_penalty > 1.0f ? repeat_penalty : 1.0f;
+    s->repeat_last_n = repeat_last_n > 0 ? repeat_last_n : 0;
+    if (seed == 0) seed = (uint64_t)time(NULL) * 2654435761u + 0x1234567u;  // sample.c:58
+    s->seed_state = seed ? seed : 0x9E3779B97F4A7C15ull;
+    s->rng_dirty = 1;
+    int rc = sync_config(s);
+    if (rc == QUASAR_OK && s->d_meta &&
+        cudaMemsetAsync(s->d_meta, 0, 2 * sizeof(int32_t), s->stream) != cudaSuccess)
+        rc = QUASAR_ECUDA;
+    set_err(s, rc);
+}
+
+void quasar_sampler_reset(quasar_sampler* s) {
+    if (!s) return;
+    int rc = ensure_device(s);
+    if (rc == QUASAR_OK &&
+        cudaMemsetAsync(s->d_meta, 0, 2 * sizeof(int32_t), s->stream) != cudaSuccess)
+        rc = QUASAR_ECUDA;
+    set_err(s, rc);
+}
+
+int quasar_sampler_last_error(const quasar_sampler* s) { return s ? s->last_error : QUASAR_EINVAL; }
+
+int quasar_sampler_pick(quasar_sampler* s, const float* logits, int n_vocab) {
+    if (!s) return -1;
+    if (n_vocab <= 0) return 0;  // sample.c:112
+    if (!logits || n_vocab > QUASAR_MAX_VOCAB) {
+        set_err(s, QUASAR_EINVAL);
+        return -1;
+    }
+    int rc = sync_config(s);
+    if (rc != QUASAR_OK) return set_err(s, rc), -1;
+
+    const float* d_in = logits;
+    cudaPointerAttributes attr;
+    const bool on_device = cudaPointerGetAttributes(&attr, logits) == cudaSuccess &&
+                           (attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged);
+    cudaGetLastError();  // clear a benign error from the attribute query
+    if (!on_device) {
+        if (s->logits_cap < n_vocab) {
+            cudaFree(s->d_logits);
+            s->d_logits = nullptr;
+            s->logits_cap = 0;
+            if (cudaMalloc(&s->d_logits, (size_t)n_vocab * sizeof(float)) != cudaSuccess)
+                return set_err(s, QUASAR_ENOMEM), -1;
+            s->logits_cap = n_vocab;
+        }
+        if (cudaMemcpyAsync(s->d_logits, logits, (size_t)n_vocab * sizeof(float),
+                            cudaMemcpyHostToDevice, s->stream) != cudaSuccess)
+            return set_err(s, QUASAR_ECUDA), -1;
+        d_in = s->d_logits;
+    }
+    quasar_sample_params p;
+    p.temperature = s->temperature;
+    p.top_p = s->top_p;
+    p.min_p = s->min_p;
+    p.repeat_penalty = s->repeat_penalty;
+    p.top_k = s->top_k;
+    p.reserved = 0;
+    rc = quasar_sampler_pick_batch(d_in, n_vocab, 1, n_vocab, nullptr, &p, s->d_rng, s->d_hist,
+                                   s->hist_cap, s->d_meta, s->d_meta + 1, 1, s->d_meta + 2,
+                                   nullptr, 0, s->stream);
+    if (rc != QUASAR_OK) return set_err(s, rc), -1;
+    if (cudaMemcpyAsync(s->h_id, s->d_meta + 2, sizeof(int32_t), cudaMemcpyDeviceToHost,
+                        s->stream) != cudaSuccess ||
+        cudaStreamSynchronize(s->stream) != cudaSuccess)
+        return set_err(s, QUASAR_ECUDA), -1;
+    set_err(s, QUASAR_OK);
+    return *s->h_id;
+}
+
+}  // extern "C"

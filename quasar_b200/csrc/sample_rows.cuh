@@ -1,0 +1,35 @@
+// sample_rows.cuh - launcher of the batched row sampler (sample_rows.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/quasar_sampler.h"
+
+namespace qs {
+
+struct RowsArgs {
+    const float* logits;
+    int64_t ld;
+    int B, V;
+    const quasar_sample_params* d_params;
+    quasar_sample_params h_params;
+    uint64_t* rng;
+    int32_t* hist;
+    int hist_cap;
+    int32_t* hist_len;
+    int32_t* hist_head;
+    int record;
+    int32_t* out;
+    quasar_pick_diag* diag;
+    int flags;
+    int vec;     // rows 16-byte aligned with ld % 4 == 0
+    int nwords;  // bitset words (set by the launcher)
+};
+
+size_t rows_smem_bytes(int V);
+int rows_threads();
+cudaError_t launch_sample_rows(const RowsArgs& args, int grid, cudaStream_t stream);
+
+}  // namespace qs
