@@ -262,11 +262,12 @@ def run_ours(args) -> None:
     ms_max = float(t.item())
 
     # ---- end to end through the public API, host buffers ----
-    e2e_steps = max(1, min(args.steps, 5))
-    host = torch.empty(B, V, dtype=torch.float32, pin_memory=True)
-    host.copy_(logits)
-    ids_host = torch.empty(B, dtype=torch.int32, pin_memory=True)
-    stage = torch.empty_like(logits)
+    e2e_steps = 0 if args.no_e2e else max(1, min(args.steps, 5))
+    if e2e_steps:
+        host = torch.empty(B, V, dtype=torch.float32, pin_memory=True)
+        host.copy_(logits)
+        ids_host = torch.empty(B, dtype=torch.int32, pin_memory=True)
+        stage = torch.empty_like(logits)
     h2d = B * V * 4
     d2h = B * 4
     barrier()
@@ -300,7 +301,8 @@ def run_ours(args) -> None:
                          "frac": achieved / peak, "traffic": traffic,
                          "peak_source": peak_kind,
                          "algorithmic_bytes_per_launch": B * BYTES_PER_ROW},
-            "e2e": {"value": B * world * e2e_steps / (e2e_ms / 1e3), "unit": "rows/s",
+            "e2e": None if not e2e_steps else {
+                    "value": B * world * e2e_steps / (e2e_ms / 1e3), "unit": "rows/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": args.steps * q.lib().quasar_sampler_pick_batch_launches(),
             "clocks": clk}
@@ -325,7 +327,10 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rows", type=int, default=B, help="rows per GPU (profiling runs use fewer)")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg (profiling)")
     args = ap.parse_args()
+    globals()["B"] = args.rows
     if args.impl == "reference":
         run_reference_arm(args)
     else:
