@@ -99,6 +99,9 @@ typedef struct {
 /* Flags for quasar_sampler_pick_batch. */
 #define QUASAR_FLAG_EXACT_SELECT  1  /* route every stochastic row through the
                                         radix-select path (same results; slower) */
+#define QUASAR_FLAG_NO_TMA        2  /* use the one-CTA-per-row register-load kernel
+                                        even where the bulk-copy ring applies
+                                        (same results) */
 
 /* Sample B rows of d_logits (row r at d_logits + r*ld, V columns, fp32).
  *   d_params    [B] per-row parameters on the device, or NULL to use *h_params
@@ -113,8 +116,10 @@ typedef struct {
  *               does (needs d_hist_len and d_hist_head).
  *   d_out       [B] chosen ids.
  *   d_diag      [B] optional report, or NULL.
- * Requirements: 1 <= V <= QUASAR_MAX_VOCAB, ld >= V. Rows whose start is
- * 16-byte aligned with ld % 4 == 0 take the vectorised loads. Finite logits
+ * Requirements: 1 <= V <= QUASAR_MAX_VOCAB, ld >= V. When the rows start
+ * 16-byte aligned with ld % 4 == 0 and V % 4 == 0, persistent CTAs stream them
+ * through a shared-memory ring filled by bulk copies (TMA); otherwise one CTA
+ * per row reads them with 256-bit (32-byte aligned rows) or scalar loads. Finite logits
  * only (as in the reference, NaN/inf give unspecified picks). Asynchronous on
  * `stream`; returns after the launch. Replaces, batched, sample.h:29. */
 #define QUASAR_MAX_VOCAB (1 << 20)
@@ -128,7 +133,9 @@ int quasar_sampler_pick_batch(const float *d_logits, int64_t ld, int B, int V,
                               int32_t *d_out, quasar_pick_diag *d_diag,
                               int flags, void *stream);
 
-/* Number of kernel launches one quasar_sampler_pick_batch call makes (1). */
+/* Number of kernel launches one quasar_sampler_pick_batch call makes (1). A
+ * row whose id comes back -1 hit the bounded-wait timeout of the bulk-copy
+ * ring (a device fault, not a sampling result). */
 int quasar_sampler_pick_batch_launches(void);
 
 /* ---- synthetic inputs (benchmark / test utility, not in the reference) ---- */

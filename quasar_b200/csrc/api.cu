@@ -118,7 +118,9 @@ int quasar_sampler_pick_batch(const float* d_logits, int64_t ld, int B, int V,
     if (!d_logits || !d_rng || !d_out || (!d_params && !h_params)) return QUASAR_EINVAL;
     if (hist_cap < 0 || (hist_cap > 0 && !d_hist)) return QUASAR_EINVAL;
     if (record && hist_cap > 0 && (!d_hist_len || !d_hist_head)) return QUASAR_EINVAL;
-    if (qs::rows_smem_bytes(V) > 220 * 1024) return QUASAR_EUNSUPPORTED;
+    const bool tma = ((uintptr_t)d_logits % 16 == 0) && (ld % 4 == 0) && (V % 4 == 0) &&
+                     qs::rows_tma_smem_bytes(V) <= 220 * 1024;
+    if (!tma && qs::rows_smem_bytes(V) > 220 * 1024) return QUASAR_EUNSUPPORTED;
     qs::RowsArgs a;
     memset(&a, 0, sizeof a);
     a.logits = d_logits;
@@ -136,7 +138,8 @@ int quasar_sampler_pick_batch(const float* d_logits, int64_t ld, int B, int V,
     a.out = d_out;
     a.diag = d_diag;
     a.flags = flags;
-    a.vec = ((uintptr_t)d_logits % 16 == 0) && (ld % 4 == 0);
+    a.vec = ((uintptr_t)d_logits % 32 == 0) && (ld % 8 == 0);
+    a.tma = tma && !(flags & QUASAR_FLAG_NO_TMA);
     const cudaError_t err = qs::launch_sample_rows(a, B, (cudaStream_t)stream);
     return err == cudaSuccess ? QUASAR_OK : QUASAR_ECUDA;
 }

@@ -1,21 +1,36 @@
-// sample_rows.cu - batched token sampler for sm_100a: one CTA per logits row.
+// sample_rows.cu - batched token sampler for sm_100a.
 //
-// Replaces franzvill/quasar sample.c:111-178 (quasar_sampler_pick), batched.
-// Per row, in sample.c's order:
+// Replaces franzvill/quasar sample.c:111-178 (quasar_sampler_pick), batched:
+// every row of a [B, V] fp32 logits matrix is sampled exactly as sample.c
+// samples one row, in sample.c's order:
 //   1. history ring -> shared-memory bitset of penalized ids (sample.c:120)
-//   2. ONE streaming pass over the row in HBM (128-bit loads): penalty
-//      (sample.c:124), temperature scale (sample.c:137,142), running max, online
-//      window sum of exp(sc - running max) in double (sample.c:147), and - when
-//      min_p > 0 - collection of every element that can survive the min-p cut
-//      into a shared-memory candidate list.
+//   2. ONE pass over the row from HBM: penalty (sample.c:124), temperature scale
+//      (sample.c:137,142), running max, online window sum of exp(sc - running
+//      max) in double (sample.c:147), and - when min_p > 0 - collection of every
+//      element that can survive the min-p cut into warp-private candidate lists.
+//      Elements more than 30 below the running max contribute < e^-30 each to
+//      that sum instead of being dropped (relative effect < V*e^-30 in the worst
+//      case, ~1e-11 on realistic rows).
 //   3. candidate path: exact p = (float)exp(sc - max) * (float)(1/sum) for the
 //      candidates, bitonic sort by (p desc, id asc) (= glibc's stable qsort of
 //      sample.c:151), top-k / top-p / min-p cuts and the inverse-CDF draw with
 //      the row's xorshift64* state (sample.c:153-177).
-//   4. select path (any parameters, or when the candidate list overflows):
+//   4. select path (any parameters, or when the candidate lists overflow): an
 //      exact radix select over the p keys of the whole row, re-reading it.
 // Greedy rows (temperature <= 0) take one pass: penalized argmax, first index
 // on ties, no PRNG step (sample.c:130-134).
+//
+// Two kernels share the per-row code:
+//   sample_rows_tma  persistent CTAs of 8 consumer warps + 1 producer warp. The
+//                    producer streams the rows' 16 KB chunks with cp.async.bulk
+//                    (TMA, no multicast) into a 4-stage shared-memory ring
+//                    guarded by mbarriers, running ahead into the next row
+//                    while the consumers finish the current one. Needs rows
+//                    that start 16-byte aligned and V % 4 == 0.
+//   sample_rows_ldg  one CTA per row, 256-bit register loads with a one-tile
+//                    prefetch; any alignment and V.
+// Every mbarrier wait is bounded (clock64); a timeout sets the abort flag, the
+// rows report id -1 and the kernel runs to its end.
 #include <math.h>
 
 #include "common.cuh"
@@ -24,14 +39,19 @@
 namespace qs {
 namespace rows {
 
-constexpr int THREADS = 256;
-constexpr int WARPS = THREADS / 32;
-constexpr int UNROLL = 4;                  // float4 loads in flight per thread per tile
-constexpr int TILE_Q = THREADS * UNROLL;   // float4 groups per tile
-constexpr int CAP = 4096;                  // candidate list capacity (entries)
-constexpr int NB = 1024;                   // radix bins per level (10 bits)
+constexpr int CONSUMERS = 256;                 // consumer threads per CTA (8 warps)
+constexpr int CWARPS = CONSUMERS / 32;
+constexpr int OCT_TILE = 2 * CONSUMERS;        // 32-byte octets per tile
+constexpr int TILE_ELEMS = 8 * OCT_TILE;       // 4096 elements per tile / chunk
+constexpr int TILE_BYTES = 4 * TILE_ELEMS;     // 16 KB
+constexpr int NSTAGE = 4;                      // ring depth of the TMA kernel
+constexpr int CAP = 2048;                      // candidate entries per row
+constexpr int CAPW = CAP / CWARPS;             // per-warp region (256)
+constexpr int KREG = CAPW / 32;                // entries per lane when a region is moved
+constexpr int NB = 1024;                       // radix bins per level (10 bits)
+constexpr long long WAIT_CYCLES = 1ll << 32;   // ~2 s: bound on any mbarrier wait
 
-// The select path reuses the candidate list storage as histograms.
+// The select path reuses the candidate storage as histograms.
 struct Hist {
     uint32_t cnt1[NB];
     unsigned long long mass1[NB];
@@ -39,15 +59,15 @@ struct Hist {
     unsigned long long mass2[NB];
     int32_t minid2[NB];
 };
-static_assert(sizeof(Hist) <= CAP * sizeof(uint64_t), "histograms fit the candidate list");
+constexpr int SCRATCH_BYTES = sizeof(Hist) > CAP * 8 ? (int)sizeof(Hist) : CAP * 8;
 
 struct Shared {
     unsigned int maxkey;  // ord_key of the largest scaled logit published so far
-    int cnt;              // candidates appended
-    float rf[WARPS];
-    double rd[WARPS];
-    int ri[WARPS];
-    unsigned long long ru[WARPS];
+    int abort;            // a bounded wait gave up
+    int wcnt[CWARPS];     // candidates per warp region (-1: overflow)
+    float rf[CWARPS];
+    double rd[CWARPS];
+    int ri[CWARPS];
     // broadcast slots
     int bin_found, bin;
     unsigned long long bin_mass_above;
@@ -57,34 +77,80 @@ struct Shared {
     float res_p;
 };
 
+// Barrier of the 256 consumer threads (warps 0-7); the TMA producer warp never
+// takes part, so it can run ahead into the next row.
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// ---- mbarrier / bulk-copy primitives (PTX ISA: mbarrier, cp.async.bulk) ----
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: false after WAIT_CYCLES without the phase completing.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity))
+        if (clock64() - t0 > WAIT_CYCLES) return false;
+    return true;
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
 // Mass fixed point: p * 2^62 truncated (p <= 1, row sums stay below 2^64).
 __device__ __forceinline__ unsigned long long fixp(uint32_t pkey) {
     return __float2ull_rz(__fmul_rn(__uint_as_float(pkey), 4611686018427387904.0f));
 }
 
-__device__ __forceinline__ float4 load4(const float* row, int q, int V, bool vec) {
-    const int e = q * 4;
-    if (vec && e + 3 < V) return __ldcs(reinterpret_cast<const float4*>(row) + q);
-    float4 v;
-    v.x = (e + 0 < V) ? __ldcs(row + e + 0) : -INFINITY;
-    v.y = (e + 1 < V) ? __ldcs(row + e + 1) : -INFINITY;
-    v.z = (e + 2 < V) ? __ldcs(row + e + 2) : -INFINITY;
-    v.w = (e + 3 < V) ? __ldcs(row + e + 3) : -INFINITY;
-    return v;
-}
-
-__device__ __forceinline__ void apply_pen(float4& v, const uint32_t* bits, int q, float rp) {
-    const uint32_t nib = (bits[q >> 3] >> ((q & 7) << 2)) & 0xFu;
-    if (nib) {
-        if (nib & 1u) v.x = penalize(v.x, rp);
-        if (nib & 2u) v.y = penalize(v.y, rp);
-        if (nib & 4u) v.z = penalize(v.z, rp);
-        if (nib & 8u) v.w = penalize(v.w, rp);
+// One 32-byte octet of a row (elements 8o..8o+7) from global memory: a single
+// 256-bit load when the row is 32-byte aligned (sm_100 ld.global.v8), else
+// masked scalar loads; elements past V read as -inf.
+__device__ __forceinline__ void load_oct(const float* row, int o, int V, bool vec, float* v) {
+    const int e = o * 8;
+    if (vec && e + 7 < V) {
+        asm volatile("ld.global.nc.L1::no_allocate.L2::evict_first.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                     : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]),
+                       "=f"(v[6]), "=f"(v[7])
+                     : "l"(row + e));
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = (e + k < V) ? __ldcs(row + e + k) : -INFINITY;
     }
 }
 
-// p key of one penalized logit: bits of p = (float)exp(sc - M) * inv, 0 outside
-// the window. The same function serves both paths, so they agree bit for bit.
+// Penalty for the octet whose bitset byte is `m` (bit k = element 8o+k).
+__device__ __forceinline__ void apply_pen_oct(float* v, uint32_t m, float rp) {
+#pragma unroll
+    for (int k = 0; k < 8; k++)
+        if (m & (1u << k)) v[k] = penalize(v[k], rp);
+}
+
+// p key of one penalized, scaled logit: bits of p = (float)exp(sc - M) * inv,
+// 0 outside the window. Both paths use it, so they agree bit for bit.
 __device__ __forceinline__ uint32_t p_key(float sc, float M, float thr, float inv) {
     if (!(sc >= thr)) return 0u;
     const float e = __double2float_rn(exp((double)__fsub_rn(sc, M)));
@@ -94,33 +160,33 @@ __device__ __forceinline__ uint32_t p_key(float sc, float M, float thr, float in
 __device__ float block_max_f(float v, Shared& s) {
     v = warp_max(v);
     if ((threadIdx.x & 31) == 0) s.rf[threadIdx.x >> 5] = v;
-    __syncthreads();
+    csync();
     float r = s.rf[0];
 #pragma unroll
-    for (int i = 1; i < WARPS; i++) r = fmaxf(r, s.rf[i]);
-    __syncthreads();
+    for (int i = 1; i < CWARPS; i++) r = fmaxf(r, s.rf[i]);
+    csync();
     return r;
 }
 
 __device__ double block_sum_d(double v, Shared& s) {
     v = warp_sum(v);
     if ((threadIdx.x & 31) == 0) s.rd[threadIdx.x >> 5] = v;
-    __syncthreads();
+    csync();
     double r = 0.0;
 #pragma unroll
-    for (int i = 0; i < WARPS; i++) r += s.rd[i];
-    __syncthreads();
+    for (int i = 0; i < CWARPS; i++) r += s.rd[i];
+    csync();
     return r;
 }
 
 __device__ int block_sum_i(int v, Shared& s) {
     v = warp_sum(v);
     if ((threadIdx.x & 31) == 0) s.ri[threadIdx.x >> 5] = v;
-    __syncthreads();
+    csync();
     int r = 0;
 #pragma unroll
-    for (int i = 0; i < WARPS; i++) r += s.ri[i];
-    __syncthreads();
+    for (int i = 0; i < CWARPS; i++) r += s.ri[i];
+    csync();
     return r;
 }
 
@@ -128,15 +194,18 @@ __device__ int block_sum_i(int v, Shared& s) {
 __device__ void bitonic_desc(uint64_t* a, int n) {
     for (int k = 2; k <= n; k <<= 1) {
         for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int i = threadIdx.x; i < n; i += THREADS) {
+            for (int i = threadIdx.x; i < n; i += CONSUMERS) {
                 const int ixj = i ^ j;
                 if (ixj > i) {
                     const uint64_t x = a[i], y = a[ixj];
                     const bool desc = (i & k) == 0;
-                    if (desc ? (x < y) : (x > y)) { a[i] = y; a[ixj] = x; }
+                    if (desc ? (x < y) : (x > y)) {
+                        a[i] = y;
+                        a[ixj] = x;
+                    }
                 }
             }
-            __syncthreads();
+            csync();
         }
     }
 }
@@ -145,66 +214,65 @@ __device__ void bitonic_desc(uint64_t* a, int n) {
 // Row context shared by the passes.
 struct Row {
     const float* ptr;
-    int V, nq;
+    int V, noct, ntiles;
     bool vec, use_pen;
     float rp, inv_t, M, thr, inv;
 };
 
 // Calls f(sc, idx) for every in-range element whose scaled logit lies in
-// [s_lo, s_hi], in coalesced order (thread-interleaved float4 groups).
+// [s_lo, s_hi], reading the row from global memory in coalesced octets.
 template <class F>
-__device__ __forceinline__ void scan_row(const Row& R, const uint32_t* bits, float s_lo,
-                                         float s_hi, F&& f) {
-    for (int q = threadIdx.x; q < R.nq; q += THREADS) {
-        float4 v = load4(R.ptr, q, R.V, R.vec);
-        if (R.use_pen) apply_pen(v, bits, q, R.rp);
-        const float sc[4] = {__fmul_rn(v.x, R.inv_t), __fmul_rn(v.y, R.inv_t),
-                             __fmul_rn(v.z, R.inv_t), __fmul_rn(v.w, R.inv_t)};
+__device__ __forceinline__ void scan_row(const Row& R, const uint8_t* bits8, float s_lo, float s_hi,
+                                         F&& f) {
+    for (int o = threadIdx.x; o < R.noct; o += CONSUMERS) {
+        float v[8];
+        load_oct(R.ptr, o, R.V, R.vec, v);
+        if (R.use_pen) apply_pen_oct(v, bits8[o], R.rp);
 #pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const int idx = 4 * q + k;
-            if (idx < R.V && sc[k] >= s_lo && sc[k] <= s_hi) f(sc[k], idx);
+        for (int k = 0; k < 8; k++) {
+            const float sc = __fmul_rn(v[k], R.inv_t);
+            const int idx = 8 * o + k;
+            if (idx < R.V && sc >= s_lo && sc <= s_hi) f(sc, idx);
         }
     }
 }
 
-// Scaled-logit interval that can hold p keys in [klo, khi) (khi exclusive).
-// Computed once by thread 0 in double with a slack far above every rounding
-// step between sc and p (float subtraction, exp, product with inv).
+// Scaled-logit interval that can hold p keys in [klo, khi) (khi exclusive),
+// computed by thread 0 in double with a slack far above every rounding step
+// between sc and p (float subtraction, exp, product with inv).
 __device__ void key_range_to_sc(const Row& R, uint32_t klo, uint64_t khi, Shared& s) {
-    __syncthreads();  // earlier readers of pf_lo / pf_hi are done
+    csync();  // earlier readers of pf_lo / pf_hi are done
     if (threadIdx.x == 0) {
         const double slack = 1e-4 + 1e-6 * fabs((double)R.M);
         const double M = (double)R.M, inv = (double)R.inv;
         float lo = -INFINITY, hi = INFINITY;
         if (klo > 0u) lo = (float)(M + log((double)__uint_as_float(klo) / inv) - slack);
-        if (khi < 0x7F800000ull)
-            hi = (float)(M + log((double)__uint_as_float((uint32_t)khi) / inv) + slack);
+        if (khi < 0x7F800000ull) hi = (float)(M + log((double)__uint_as_float((uint32_t)khi) / inv) + slack);
         s.pf_lo = lo;
         s.pf_hi = hi;
     }
-    __syncthreads();
+    csync();
 }
 
 // Warp 0: first bin, scanning from the top bin down, where the running total
-// (mass or count) reaches `target`. Publishes the bin and the mass / count of
-// all higher bins. bin_found = 0 when the total stays below target.
+// (mass or count) reaches `target` (>= 1). Publishes the bin and the mass and
+// count of all higher bins; bin_found = 0 when the total stays below target.
 __device__ void find_bin(const uint32_t* cnt, const unsigned long long* mass, bool by_mass,
                          unsigned long long target, Shared& s) {
-    __syncthreads();  // earlier readers of the bin_* slots are done
+    csync();  // earlier readers of the bin_* slots are done
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
         const int hi = NB - 1 - 32 * lane;  // this lane owns bins hi, hi-1, ..., hi-31
-        unsigned long long tv = 0, tm = 0;
+        unsigned long long tm = 0;
         unsigned int tc = 0;
         for (int b = hi; b > hi - 32; b--) {
             tm += mass[b];
             tc += cnt[b];
         }
-        tv = by_mass ? tm : (unsigned long long)tc;
-        unsigned long long incl_v = warp_incl_scan(tv, lane);
-        unsigned long long incl_m = warp_incl_scan(tm, lane);
-        unsigned int incl_c = warp_incl_scan(tc, lane);
+        const unsigned long long tv = by_mass ? tm : (unsigned long long)tc;
+        const unsigned long long incl_v = warp_incl_scan(tv, lane);
+        const unsigned long long incl_m = warp_incl_scan(tm, lane);
+        const unsigned int incl_c = warp_incl_scan(tc, lane);
         const unsigned bal = __ballot_sync(FULL, incl_v >= target);
         if (bal == 0u) {
             if (lane == 0) s.bin_found = 0;
@@ -216,7 +284,10 @@ __device__ void find_bin(const uint32_t* cnt, const unsigned long long* mass, bo
                 int found = hi - 31;
                 for (int b = hi; b > hi - 32; b--) {
                     const unsigned long long v = by_mass ? mass[b] : (unsigned long long)cnt[b];
-                    if (av + v >= target) { found = b; break; }
+                    if (av + v >= target) {
+                        found = b;
+                        break;
+                    }
                     av += v;
                     am += mass[b];
                     ac += cnt[b];
@@ -228,28 +299,28 @@ __device__ void find_bin(const uint32_t* cnt, const unsigned long long* mass, bo
             }
         }
     }
-    __syncthreads();
+    csync();
 }
 
 __device__ void zero_level2(Hist* H) {
-    for (int i = threadIdx.x; i < NB; i += THREADS) {
+    for (int i = threadIdx.x; i < NB; i += CONSUMERS) {
         H->cnt2[i] = 0u;
         H->mass2[i] = 0ull;
         H->minid2[i] = 0x7FFFFFFF;
     }
-    __syncthreads();
+    csync();
 }
 
 // Histogram of key bits [shift, shift+10) over the elements whose key has
 // prefix `prefix` above bit shift+10.
-__device__ void refine(const Row& R, const uint32_t* bits, Hist* H, uint32_t prefix, int shift,
+__device__ void refine(const Row& R, const uint8_t* bits8, Hist* H, uint32_t prefix, int shift,
                        Shared& s) {
     zero_level2(H);
     const uint32_t klo = prefix << (shift + 10);
     const uint64_t khi = (uint64_t)(prefix + 1) << (shift + 10);
     key_range_to_sc(R, klo, khi, s);
     const float s_lo = s.pf_lo, s_hi = s.pf_hi;
-    scan_row(R, bits, s_lo, s_hi, [&](float sc, int idx) {
+    scan_row(R, bits8, s_lo, s_hi, [&](float sc, int idx) {
         const uint32_t key = p_key(sc, R.M, R.thr, R.inv);
         if (key != 0u && (key >> (shift + 10)) == prefix) {
             const int b = (key >> shift) & (NB - 1);
@@ -258,22 +329,22 @@ __device__ void refine(const Row& R, const uint32_t* bits, Hist* H, uint32_t pre
             atomicMin(&H->minid2[b], idx);
         }
     });
-    __syncthreads();
+    csync();
 }
 
 struct Sel {
     int found;
-    int rank;            // position in (p desc, id asc) order
-    uint32_t key;        // p key of that position
-    int t;               // index inside the group of equal keys (id order)
-    int minid;           // smallest id with this key
+    int rank;                    // position in (p desc, id asc) order
+    uint32_t key;                // p key of that position
+    int t;                       // index inside the group of equal keys (id order)
+    int minid;                   // smallest id with this key
     unsigned long long m_above;  // mass of strictly larger keys
     unsigned int c_above;        // count of strictly larger keys
 };
 
 // Exact select over the row: by_mass -> smallest rank whose cumulative mass
 // reaches target; otherwise the element of rank target-1 (target = rank + 1).
-__device__ Sel select_row(const Row& R, const uint32_t* bits, Hist* H, bool by_mass,
+__device__ Sel select_row(const Row& R, const uint8_t* bits8, Hist* H, bool by_mass,
                           unsigned long long target, Shared& s) {
     Sel out = {};
     if (by_mass && target == 0ull) target = 1ull;  // every window element carries mass >= 1
@@ -285,7 +356,7 @@ __device__ Sel select_row(const Row& R, const uint32_t* bits, Hist* H, bool by_m
     int n_eq = 0, minid = 0;
     for (int level = 0; level < 2; level++) {
         const int shift = level == 0 ? 10 : 0;
-        refine(R, bits, H, prefix, shift, s);
+        refine(R, bits8, H, prefix, shift, s);
         const unsigned long long rem = target - (by_mass ? m_above : (unsigned long long)c_above);
         find_bin(H->cnt2, H->mass2, by_mass, rem, s);
         if (!s.bin_found) return out;  // unreachable for consistent histograms
@@ -294,7 +365,7 @@ __device__ Sel select_row(const Row& R, const uint32_t* bits, Hist* H, bool by_m
         c_above += s.bin_cnt_above;
         n_eq = (int)H->cnt2[s.bin];
         minid = H->minid2[s.bin];
-        __syncthreads();
+        csync();
     }
     out.found = 1;
     out.key = prefix;
@@ -304,7 +375,7 @@ __device__ Sel select_row(const Row& R, const uint32_t* bits, Hist* H, bool by_m
     if (by_mass) {
         const unsigned long long pf = fixp(prefix);
         const unsigned long long rem = target - m_above;
-        long long t = pf ? (long long)((rem + pf - 1) / pf) - 1 : 0;
+        const long long t = pf ? (long long)((rem + pf - 1) / pf) - 1 : 0;
         out.t = (int)min(max(t, 0ll), (long long)(n_eq - 1));
     } else {
         out.t = (int)(target - 1 - c_above);
@@ -313,68 +384,62 @@ __device__ Sel select_row(const Row& R, const uint32_t* bits, Hist* H, bool by_m
     return out;
 }
 
-// Id of the t-th element (ascending id) whose key equals `key`.
-__device__ int resolve_id(const Row& R, const uint32_t* bits, const Sel& sel, Shared& s) {
+// Id of the t-th element (ascending id) whose key equals sel.key.
+__device__ int resolve_id(const Row& R, const uint8_t* bits8, const Sel& sel, Shared& s) {
     if (sel.t == 0) return sel.minid;
     key_range_to_sc(R, sel.key, (uint64_t)sel.key + 1, s);
     const float s_lo = s.pf_lo, s_hi = s.pf_hi;
-    // each thread owns a contiguous run of float4 groups
-    const int per = (R.nq + THREADS - 1) / THREADS;
-    const int q0 = threadIdx.x * per, q1 = min(q0 + per, R.nq);
+    // each thread owns a contiguous run of octets
+    const int per = (R.noct + CONSUMERS - 1) / CONSUMERS;
+    const int o0 = threadIdx.x * per, o1 = min(o0 + per, R.noct);
+    auto match = [&](float l, int idx) {
+        const float sc = __fmul_rn(l, R.inv_t);
+        return idx < R.V && sc >= s_lo && sc <= s_hi && p_key(sc, R.M, R.thr, R.inv) == sel.key;
+    };
     int mine = 0;
-    for (int q = q0; q < q1; q++) {
-        float4 v = load4(R.ptr, q, R.V, R.vec);
-        if (R.use_pen) apply_pen(v, bits, q, R.rp);
-        const float l[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const float sc = __fmul_rn(l[k], R.inv_t);
-            if (4 * q + k < R.V && sc >= s_lo && sc <= s_hi && p_key(sc, R.M, R.thr, R.inv) == sel.key)
-                mine++;
-        }
+    for (int o = o0; o < o1; o++) {
+        float v[8];
+        load_oct(R.ptr, o, R.V, R.vec, v);
+        if (R.use_pen) apply_pen_oct(v, bits8[o], R.rp);
+        for (int k = 0; k < 8; k++) mine += match(v[k], 8 * o + k) ? 1 : 0;
     }
-    // exclusive block scan of `mine`
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int incl = warp_incl_scan(mine, lane);
     if (lane == 31) s.ri[w] = incl;
-    __syncthreads();
+    csync();
     int before = incl - mine;
     for (int i = 0; i < w; i++) before += s.ri[i];
     if (sel.t >= before && sel.t < before + mine) {
         int want = sel.t - before;
-        for (int q = q0; q < q1 && want >= 0; q++) {
-            float4 v = load4(R.ptr, q, R.V, R.vec);
-            if (R.use_pen) apply_pen(v, bits, q, R.rp);
-            const float l[4] = {v.x, v.y, v.z, v.w};
-            for (int k = 0; k < 4; k++) {
-                const float sc = __fmul_rn(l[k], R.inv_t);
-                if (4 * q + k < R.V && sc >= s_lo && sc <= s_hi &&
-                    p_key(sc, R.M, R.thr, R.inv) == sel.key) {
-                    if (want == 0) s.res_pos = 4 * q + k;
+        for (int o = o0; o < o1 && want >= 0; o++) {
+            float v[8];
+            load_oct(R.ptr, o, R.V, R.vec, v);
+            if (R.use_pen) apply_pen_oct(v, bits8[o], R.rp);
+            for (int k = 0; k < 8 && want >= 0; k++) {
+                if (match(v[k], 8 * o + k)) {
+                    if (want == 0) s.res_pos = 8 * o + k;
                     want--;
-                    if (want < 0) break;
                 }
             }
         }
     }
-    __syncthreads();
+    csync();
     const int id = s.res_pos;
-    __syncthreads();
+    csync();
     return id;
 }
 
 // Select path: exact cuts and draw over the whole row. Publishes res_id,
 // res_nc, res_p.
-__device__ void select_path(const Row& R, const uint32_t* bits, Hist* H, const RowParams& P,
-                            double u, Shared& s) {
-    // level-1 histogram over all window elements
-    for (int i = threadIdx.x; i < NB; i += THREADS) {
+__device__ void select_path(const Row& R, const uint8_t* bits8, Hist* H,
+                                         const RowParams& P, double u, Shared& s) {
+    for (int i = threadIdx.x; i < NB; i += CONSUMERS) {
         H->cnt1[i] = 0u;
         H->mass1[i] = 0ull;
     }
-    __syncthreads();
+    csync();
     int nw_local = 0;
-    scan_row(R, bits, R.thr, INFINITY, [&](float sc, int idx) {
+    scan_row(R, bits8, R.thr, INFINITY, [&](float sc, int) {
         const uint32_t key = p_key(sc, R.M, R.thr, R.inv);
         if (key != 0u) {
             atomicAdd(&H->cnt1[key >> 20], 1u);
@@ -389,9 +454,8 @@ __device__ void select_path(const Row& R, const uint32_t* bits, Hist* H, const R
     // top-p (sample.c:156-160)
     int nc2 = nc1;
     if (P.top_p < 1.0f) {
-        const unsigned long long tgt =
-            (unsigned long long)ceil((double)P.top_p * 4611686018427387904.0);
-        const Sel sp = select_row(R, bits, H, true, tgt, s);
+        const unsigned long long tgt = (unsigned long long)ceil((double)P.top_p * 4611686018427387904.0);
+        const Sel sp = select_row(R, bits8, H, true, tgt, s);
         if (sp.found && sp.rank < nc1) nc2 = sp.rank + 1;
     }
     // min-p (sample.c:162-167): keep = min(nc, max(1, #{p >= min_p * p_max}))
@@ -401,13 +465,13 @@ __device__ void select_path(const Row& R, const uint32_t* bits, Hist* H, const R
         const uint32_t fk = __float_as_uint(floor_p);
         const uint32_t fb = fk >> 20;
         int above = 0;
-        for (int b = threadIdx.x; b < NB; b += THREADS)
+        for (int b = threadIdx.x; b < NB; b += CONSUMERS)
             if ((uint32_t)b > fb) above += (int)H->cnt1[b];
         int in_bin = 0;
         if (fb < (uint32_t)NB) {
             key_range_to_sc(R, fk, (uint64_t)(fb + 1) << 20, s);
             const float s_lo = s.pf_lo, s_hi = s.pf_hi;
-            scan_row(R, bits, s_lo, s_hi, [&](float sc, int) {
+            scan_row(R, bits8, s_lo, s_hi, [&](float sc, int) {
                 const uint32_t key = p_key(sc, R.M, R.thr, R.inv);
                 if (key >= fk && (key >> 20) == fb) in_bin++;
             });
@@ -418,30 +482,29 @@ __device__ void select_path(const Row& R, const uint32_t* bits, Hist* H, const R
     if (nc < 1) nc = 1;
 
     // the last kept element and the kept mass
-    const Sel last = select_row(R, bits, H, false, (unsigned long long)nc, s);
-    const unsigned long long rsum_fix =
-        last.m_above + (unsigned long long)(last.t + 1) * fixp(last.key);
+    const Sel last = select_row(R, bits8, H, false, (unsigned long long)nc, s);
+    const unsigned long long rsum_fix = last.m_above + (unsigned long long)(last.t + 1) * fixp(last.key);
     const double rsum = (double)rsum_fix * (1.0 / 4611686018427387904.0);
     const double r = u * rsum;
     const unsigned long long tgt = (unsigned long long)ceil(r * 4611686018427387904.0);
-    Sel d = select_row(R, bits, H, true, tgt, s);
+    Sel d = select_row(R, bits8, H, true, tgt, s);
     if (!d.found || d.rank >= nc) d = last;
-    const int id = resolve_id(R, bits, d, s);
+    const int id = resolve_id(R, bits8, d, s);
     if (threadIdx.x == 0) {
         s.res_id = id;
         s.res_nc = nc;
         s.res_p = __uint_as_float(d.key);
     }
-    __syncthreads();
+    csync();
 }
 
-// Candidate path over the sorted list keys[0, nk): cuts, draw. Warp 0 only.
+// Candidate path over the sorted list keys[0, nk): cuts and draw. Warp 0 only.
 __device__ void candidate_cuts(const uint64_t* keys, int nk, const RowParams& P, float floor_p,
                                double u, Shared& s) {
     const int lane = threadIdx.x & 31;
     auto pval = [&](int i) { return __uint_as_float((uint32_t)(keys[i] >> 32)); };
     const int BEYOND = 0x7FFFFFFF;
-    // top-k: a cut inside the list is exact; a larger k is beyond the min-p cut
+    // top-k: a cut inside the list is exact; a larger k lies beyond the min-p cut
     const int nc1 = (P.top_k > 0 && P.top_k < nk) ? P.top_k : BEYOND;
     const int lim = min(nc1, nk);
     int nc2 = nc1;
@@ -452,7 +515,10 @@ __device__ void candidate_cuts(const uint64_t* keys, int nk, const RowParams& P,
             const double p = i < lim ? (double)pval(i) : 0.0;
             const double c = warp_incl_scan(p, lane) + carry;
             const unsigned bal = __ballot_sync(FULL, i < lim && c >= (double)P.top_p);
-            if (bal) { nc2 = base + __ffs(bal); break; }
+            if (bal) {
+                nc2 = base + __ffs(bal);
+                break;
+            }
             carry = __shfl_sync(FULL, c, 31);
         }
     }
@@ -462,7 +528,10 @@ __device__ void candidate_cuts(const uint64_t* keys, int nk, const RowParams& P,
     for (int base = 0; base < nk; base += 32) {
         const int i = base + lane;
         const unsigned bal = __ballot_sync(FULL, i >= 1 && i < nk && pval(i) < floor_p);
-        if (bal) { fb = base + __ffs(bal) - 1; break; }
+        if (bal) {
+            fb = base + __ffs(bal) - 1;
+            break;
+        }
     }
     int nc = min(nc2, fb);
     if (nc < 1) nc = 1;
@@ -478,7 +547,10 @@ __device__ void candidate_cuts(const uint64_t* keys, int nk, const RowParams& P,
         const double p = i < nc ? (double)pval(i) : 0.0;
         const double c = warp_incl_scan(p, lane) + carry;
         const unsigned bal = __ballot_sync(FULL, i < nc && c >= r);
-        if (bal) { chosen = base + __ffs(bal) - 1; break; }
+        if (bal) {
+            chosen = base + __ffs(bal) - 1;
+            break;
+        }
         carry = __shfl_sync(FULL, c, 31);
     }
     if (lane == 0) {
@@ -488,265 +560,512 @@ __device__ void candidate_cuts(const uint64_t* keys, int nk, const RowParams& P,
     }
 }
 
-__global__ void __launch_bounds__(THREADS, 4) sample_rows_kernel(RowsArgs a) {
-    extern __shared__ __align__(16) unsigned char dyn[];
-    uint64_t* buf = reinterpret_cast<uint64_t*>(dyn);
-    uint32_t* bits = reinterpret_cast<uint32_t*>(dyn + CAP * sizeof(uint64_t));
-    Hist* H = reinterpret_cast<Hist*>(dyn);
-    __shared__ Shared s;
-    const int tid = threadIdx.x;
+// Drops the entries of a warp's candidate region whose scaled logit is below
+// tau; returns the new count (warp-uniform).
+__device__ int warp_prune(uint64_t* region, int cnt, float tau, int lane) {
+    uint64_t e[KREG];
+#pragma unroll
+    for (int k = 0; k < KREG; k++) {
+        const int i = lane + 32 * k;
+        e[k] = i < cnt ? region[i] : 0ull;
+    }
+    __syncwarp();
+    int out = 0;
+#pragma unroll
+    for (int k = 0; k < KREG; k++) {
+        const int i = lane + 32 * k;
+        const bool keep = i < cnt && __uint_as_float((uint32_t)(e[k] >> 32)) >= tau;
+        const unsigned bal = __ballot_sync(FULL, keep);
+        if (keep) region[out + __popc(bal & ((1u << lane) - 1u))] = e[k];
+        out += __popc(bal);
+    }
+    __syncwarp();
+    return out;
+}
 
-    for (int i = tid; i < a.nwords; i += THREADS) bits[i] = 0u;
-    __syncthreads();
+// ---------------------------------------------------------------------------
+// Tile sources: where the consumers' 16 elements per tile come from. The
+// element -> thread mapping is the same for both: octets it*OCT_TILE + tid and
+// it*OCT_TILE + 256 + tid (index order within a thread is kept).
 
-    for (int row = blockIdx.x; row < a.B; row += gridDim.x) {
-        const RowParams P = clamp_params(a.d_params ? a.d_params[row] : a.h_params);
-        const int cap = a.hist ? a.hist_cap : 0;
-        int len = 0, head = 0;
-        const int32_t* ring = nullptr;
-        if (cap > 0) {
-            ring = a.hist + (int64_t)row * cap;
-            len = a.hist_len ? min(max(a.hist_len[row], 0), cap) : cap;
-            head = a.hist_head ? ((a.hist_head[row] % cap) + cap) % cap : 0;
+struct LdgSource {
+    float nxt[16];
+    __device__ __forceinline__ void begin(const Row& R) { load(R, 0, nxt); }
+    __device__ __forceinline__ static void load(const Row& R, int it, float* v) {
+        const int o0 = it * OCT_TILE + threadIdx.x;
+        load_oct(R.ptr, o0, R.V, R.vec, v);
+        load_oct(R.ptr, o0 + CONSUMERS, R.V, R.vec, v + 8);
+    }
+    // tile `it` into v; the next tile's loads are issued before returning
+    __device__ __forceinline__ void get(const Row& R, int it, float (&v)[16], Shared&) {
+#pragma unroll
+        for (int j = 0; j < 16; j++) v[j] = nxt[j];
+        if (it + 1 < R.ntiles) load(R, it + 1, nxt);
+    }
+    __device__ __forceinline__ void release() {}
+};
+
+struct TmaSource {
+    const float* ring;  // NSTAGE tiles
+    uint32_t full0, empty0;
+    uint32_t g;  // chunks consumed by this CTA so far
+    __device__ __forceinline__ void begin(const Row&) {}
+    __device__ __forceinline__ void get(const Row& R, int it, float (&v)[16], Shared& s) {
+        const int st = (int)(g % NSTAGE);
+        const uint32_t par = (g / NSTAGE) & 1u;
+        bool ok = *reinterpret_cast<volatile int*>(&s.abort) == 0;
+        if (ok && !mbar_wait(full0 + 8u * st, par)) {
+            s.abort = 1;
+            ok = false;
         }
-        Row R;
-        R.ptr = a.logits + (int64_t)row * a.ld;
-        R.V = a.V;
-        R.nq = (a.V + 3) >> 2;
-        R.vec = a.vec != 0;
-        R.use_pen = P.rp > 1.0f && len > 0;
-        R.rp = P.rp;
-        if (R.use_pen) {
-            for (int i = tid; i < len; i += THREADS) {
-                const int id = ring[(head + i) % cap];
-                if (id >= 0 && id < a.V) atomicOr(&bits[id >> 5], 1u << (id & 31));
+        const int tid = threadIdx.x;
+        const float* t = ring + st * TILE_ELEMS;
+        const int e0 = it * TILE_ELEMS + 8 * tid, e1 = e0 + 8 * CONSUMERS;
+        if (ok) {
+            const float4* p0 = reinterpret_cast<const float4*>(t + 8 * tid);
+            const float4* p1 = reinterpret_cast<const float4*>(t + 8 * (tid + CONSUMERS));
+            const float4 a = p0[0], b = p0[1], c = p1[0], d = p1[1];
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+            v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+            v[8] = c.x; v[9] = c.y; v[10] = c.z; v[11] = c.w;
+            v[12] = d.x; v[13] = d.y; v[14] = d.z; v[15] = d.w;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            if (!ok || e0 + k >= R.V) v[k] = -INFINITY;
+            if (!ok || e1 + k >= R.V) v[8 + k] = -INFINITY;
+        }
+    }
+    __device__ __forceinline__ void release() {
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(empty0 + 8u * (g % NSTAGE));
+        g++;
+    }
+};
+
+// ---------------------------------------------------------------------------
+// One row, all consumer threads. Returns nothing; writes out / diag / ring /
+// rng of the row.
+template <class Src>
+__device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src, uint64_t* buf,
+                                            uint32_t* bits, Shared& s) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint8_t* bits8 = reinterpret_cast<const uint8_t*>(bits);
+    Hist* H = reinterpret_cast<Hist*>(buf);
+    const RowParams P = clamp_params(a.d_params ? a.d_params[row] : a.h_params);
+    const int cap = a.hist ? a.hist_cap : 0;
+    int len = 0, head = 0;
+    const int32_t* ring = nullptr;
+    if (cap > 0) {
+        ring = a.hist + (int64_t)row * cap;
+        len = a.hist_len ? min(max(a.hist_len[row], 0), cap) : cap;
+        head = a.hist_head ? ((a.hist_head[row] % cap) + cap) % cap : 0;
+    }
+    Row R;
+    R.ptr = a.logits + (int64_t)row * a.ld;
+    R.V = a.V;
+    R.noct = (a.V + 7) >> 3;
+    R.ntiles = (R.noct + OCT_TILE - 1) / OCT_TILE;
+    R.vec = a.vec != 0;
+    R.use_pen = P.rp > 1.0f && len > 0;
+    R.rp = P.rp;
+    R.inv_t = 0.0f;
+    R.M = R.thr = R.inv = 0.0f;
+    if (R.use_pen) {
+        for (int i = tid; i < len; i += CONSUMERS) {
+            const int id = ring[(head + i) % cap];
+            if (id >= 0 && id < a.V) atomicOr(&bits[id >> 5], 1u << (id & 31));
+        }
+    }
+    if (tid == 0) s.maxkey = 0u;
+    csync();
+    src.begin(R);
+
+    int path;
+    uint64_t st_rng = 0;
+    if (P.T <= 0.0f) {
+        // ---- greedy: penalized argmax, first index on ties ----
+        float bv = -INFINITY;
+        int bi = 0x7FFFFFFF;
+        for (int it = 0; it < R.ntiles; it++) {
+            float v[16];
+            src.get(R, it, v, s);
+            const int o0 = it * OCT_TILE + tid, o1 = o0 + CONSUMERS;
+            if (R.use_pen) {
+                const uint32_t m0 = o0 < R.noct ? bits8[o0] : 0u;
+                const uint32_t m1 = o1 < R.noct ? bits8[o1] : 0u;
+                if (m0 | m1) {
+                    apply_pen_oct(v, m0, R.rp);
+                    apply_pen_oct(v + 8, m1, R.rp);
+                }
+            }
+            src.release();
+            float mt = v[0];
+#pragma unroll
+            for (int j = 1; j < 16; j++) mt = fmaxf(mt, v[j]);
+            if (mt > bv) {  // strictly larger: the first index holding mt wins
+                int j = 0;
+                while (j < 15 && !(v[j] == mt)) j++;
+                bv = mt;
+                bi = j < 8 ? 8 * o0 + j : 8 * o1 + (j - 8);
             }
         }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(FULL, bv, o);
+            const int oi = __shfl_xor_sync(FULL, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (lane == 0) {
+            s.rf[warp] = bv;
+            s.ri[warp] = bi;
+        }
+        csync();
         if (tid == 0) {
-            s.maxkey = 0u;
-            s.cnt = 0;
+            float best = s.rf[0];
+            int besti = s.ri[0];
+            for (int w = 1; w < CWARPS; w++)
+                if (s.rf[w] > best || (s.rf[w] == best && s.ri[w] < besti)) {
+                    best = s.rf[w];
+                    besti = s.ri[w];
+                }
+            s.res_id = (besti == 0x7FFFFFFF || besti >= a.V) ? 0 : besti;
+            s.res_nc = 0;
+            s.res_p = 1.0f;
         }
-        __syncthreads();
-
-        int path;
-        if (P.T <= 0.0f) {
-            // ---- greedy: penalized argmax, first index on ties ----
-            float bv = -INFINITY;
-            int bi = 0x7FFFFFFF;
-            for (int base = 0; base < R.nq; base += TILE_Q) {
-                float4 v[UNROLL];
-#pragma unroll
-                for (int u = 0; u < UNROLL; u++) {
-                    const int q = base + u * THREADS + tid;
-                    v[u] = q < R.nq ? load4(R.ptr, q, R.V, R.vec)
-                                    : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-                }
-#pragma unroll
-                for (int u = 0; u < UNROLL; u++) {
-                    const int q = base + u * THREADS + tid;
-                    if (q >= R.nq) continue;
-                    if (R.use_pen) apply_pen(v[u], bits, q, R.rp);
-                    if (v[u].x > bv) { bv = v[u].x; bi = 4 * q; }
-                    if (v[u].y > bv) { bv = v[u].y; bi = 4 * q + 1; }
-                    if (v[u].z > bv) { bv = v[u].z; bi = 4 * q + 2; }
-                    if (v[u].w > bv) { bv = v[u].w; bi = 4 * q + 3; }
+        path = QUASAR_PATH_GREEDY;
+        csync();
+    } else {
+        // ---- one streaming pass: max, online window sum, candidates ----
+        R.inv_t = __fdiv_rn(1.0f, P.T);
+        const bool collect = !(a.flags & QUASAR_FLAG_EXACT_SELECT) && P.min_p > 0.0f;
+        // every element with p >= min_p * p_max has sc >= max + cmargin (1% slack)
+        const float cmargin = collect ? (float)(log((double)fminf(P.min_p, 1.0f)) - 0.01) : 0.0f;
+        uint64_t* region = buf + warp * CAPW;
+        int wcnt = 0;  // warp-uniform; -1 after an overflow
+        float m = -INFINITY;
+        double S = 0.0;
+        for (int it = 0; it < R.ntiles; it++) {
+            float v[16];
+            src.get(R, it, v, s);
+            const int o0 = it * OCT_TILE + tid, o1 = o0 + CONSUMERS;
+            if (R.use_pen) {
+                const uint32_t m0 = o0 < R.noct ? bits8[o0] : 0u;
+                const uint32_t m1 = o1 < R.noct ? bits8[o1] : 0u;
+                if (m0 | m1) {
+                    apply_pen_oct(v, m0, R.rp);
+                    apply_pen_oct(v + 8, m1, R.rp);
                 }
             }
+            src.release();
+            // sample.c:142: sc = l * inv_t, rounded exactly like the reference
+            float sc[16];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(FULL, bv, o);
-                const int oi = __shfl_xor_sync(FULL, bi, o);
-                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+            for (int j = 0; j < 16; j++) sc[j] = __fmul_rn(v[j], R.inv_t);
+            float mt = fmaxf(fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3])),
+                             fmaxf(fmaxf(sc[4], sc[5]), fmaxf(sc[6], sc[7])));
+            mt = fmaxf(mt, fmaxf(fmaxf(fmaxf(sc[8], sc[9]), fmaxf(sc[10], sc[11])),
+                                 fmaxf(fmaxf(sc[12], sc[13]), fmaxf(sc[14], sc[15]))));
+            if (mt > m) {
+                S *= exp((double)m - (double)mt);
+                m = mt;
+                if (collect) atomicMax(&s.maxkey, ord_key(m));
             }
-            if ((tid & 31) == 0) {
-                s.rf[tid >> 5] = bv;
-                s.ri[tid >> 5] = bi;
+            if (it == 0) csync();  // first-tile maxima are published
+            if (m > -INFINITY) {
+                // sample.c:148 against the running max
+                float e[16];
+#pragma unroll
+                for (int j = 0; j < 16; j++) e[j] = expf(__fsub_rn(sc[j], m));
+#pragma unroll
+                for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+                    for (int j = 0; j < w; j++) e[j] += e[j + w];
+                S += (double)e[0];
             }
-            __syncthreads();
-            if (tid == 0) {
-                float best = s.rf[0];
-                int besti = s.ri[0];
-                for (int w = 1; w < WARPS; w++)
-                    if (s.rf[w] > best || (s.rf[w] == best && s.ri[w] < besti)) {
-                        best = s.rf[w];
-                        besti = s.ri[w];
-                    }
-                s.res_id = (besti == 0x7FFFFFFF || besti >= a.V) ? 0 : besti;
-                s.res_nc = 0;
-                s.res_p = 1.0f;
-            }
-            path = QUASAR_PATH_GREEDY;
-            R.inv = 0.0f;
-            __syncthreads();
-        } else {
-            // ---- one streaming pass: max, online window sum, candidates ----
-            R.inv_t = __fdiv_rn(1.0f, P.T);
-            const bool collect = !(a.flags & QUASAR_FLAG_EXACT_SELECT) && P.min_p > 0.0f;
-            // every element with p >= min_p * p_max has sc >= max + cmargin (1% slack)
-            const float cmargin =
-                collect ? (float)(log((double)fminf(P.min_p, 1.0f)) - 0.01) : 0.0f;
-            float m = -INFINITY;
-            double S = 0.0;
-            const int ntiles = (R.nq + TILE_Q - 1) / TILE_Q;
-            for (int it = 0; it < ntiles; it++) {
-                const int base = it * TILE_Q;
-                float4 v[UNROLL];
+            if (collect) {
+                const unsigned int mk = *reinterpret_cast<volatile unsigned int*>(&s.maxkey);
+                const float ref = mk ? fmaxf(m, ord_key_inv(mk)) : m;
+                const float tau = __fadd_rn(ref, cmargin);
+                uint32_t mask = 0u;
+                if (mt >= tau) {
 #pragma unroll
-                for (int u = 0; u < UNROLL; u++) {
-                    const int q = base + u * THREADS + tid;
-                    v[u] = q < R.nq ? load4(R.ptr, q, R.V, R.vec)
-                                    : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+                    for (int j = 0; j < 16; j++) mask |= (sc[j] >= tau ? 1u : 0u) << j;
                 }
-                float sc[4 * UNROLL];
+                if (__ballot_sync(FULL, mask != 0u) && wcnt >= 0) {
+                    // warp-private append: no shared atomics on the streaming path
+                    const int cnt = __popc(mask);
+                    const int incl = warp_incl_scan(cnt, lane);
+                    const int total = __shfl_sync(FULL, incl, 31);
+                    if (wcnt + total > CAPW) wcnt = warp_prune(region, wcnt, tau, lane);
+                    if (wcnt + total > CAPW) {
+                        wcnt = -1;  // overflow: this row takes the select path
+                    } else {
+                        int pos = wcnt + incl - cnt;
+                        if (mask) {
 #pragma unroll
-                for (int u = 0; u < UNROLL; u++) {
-                    const int q = base + u * THREADS + tid;
-                    if (R.use_pen && q < R.nq) apply_pen(v[u], bits, q, R.rp);
-                    sc[4 * u + 0] = __fmul_rn(v[u].x, R.inv_t);
-                    sc[4 * u + 1] = __fmul_rn(v[u].y, R.inv_t);
-                    sc[4 * u + 2] = __fmul_rn(v[u].z, R.inv_t);
-                    sc[4 * u + 3] = __fmul_rn(v[u].w, R.inv_t);
-                }
-                float mt = sc[0];
-#pragma unroll
-                for (int j = 1; j < 4 * UNROLL; j++) mt = fmaxf(mt, sc[j]);
-                if (mt > m) {
-                    S *= exp((double)m - (double)mt);
-                    m = mt;
-                    if (collect) atomicMax(&s.maxkey, ord_key(m));
-                }
-                if (it == 0) __syncthreads();  // first-tile maxima are published
-                if (m > -INFINITY) {
-                    const float lo = __fsub_rn(m, 30.0f);
-                    float part = 0.0f;
-#pragma unroll
-                    for (int j = 0; j < 4 * UNROLL; j++)
-                        part += (sc[j] >= lo) ? expf(__fsub_rn(sc[j], m)) : 0.0f;
-                    S += (double)part;
-                }
-                if (collect) {
-                    const unsigned int mk = *reinterpret_cast<volatile unsigned int*>(&s.maxkey);
-                    const float ref = mk ? fmaxf(m, ord_key_inv(mk)) : m;
-                    const float tau = __fadd_rn(ref, cmargin);
-#pragma unroll
-                    for (int j = 0; j < 4 * UNROLL; j++) {
-                        if (sc[j] >= tau) {
-                            const int idx = 4 * (base + (j >> 2) * THREADS + tid) + (j & 3);
-                            if (idx < R.V) {
-                                const int pos = atomicAdd(&s.cnt, 1);
-                                if (pos < CAP)
-                                    buf[pos] = ((uint64_t)__float_as_uint(sc[j]) << 32) | (uint32_t)idx;
+                            for (int j = 0; j < 16; j++) {
+                                if (mask & (1u << j)) {
+                                    const int idx = j < 8 ? 8 * o0 + j : 8 * o1 + (j - 8);
+                                    region[pos] = idx < R.V
+                                                      ? ((uint64_t)__float_as_uint(sc[j]) << 32) | (uint32_t)idx
+                                                      : ((uint64_t)0xFF800000u << 32);
+                                    pos++;
+                                }
                             }
                         }
+                        wcnt += total;
                     }
                 }
             }
-            __syncthreads();
-            R.M = block_max_f(m, s);
-            const double contrib = (m > -INFINITY) ? S * exp((double)m - (double)R.M) : 0.0;
-            const double Stot = block_sum_d(contrib, s);
-            R.inv = __double2float_rn(1.0 / Stot);
-            R.thr = __fsub_rn(R.M, 30.0f);
+        }
+        if (lane == 0) s.wcnt[warp] = wcnt;
+        R.M = block_max_f(m, s);
+        const double contrib = (m > -INFINITY) ? S * exp((double)m - (double)R.M) : 0.0;
+        const double Stot = block_sum_d(contrib, s);
+        R.inv = __double2float_rn(1.0 / Stot);
+        R.thr = __fsub_rn(R.M, 30.0f);
 
-            // PRNG draw (sample.c:173): one step per stochastic row
-            uint64_t st = a.rng[row];
-            const double u = rng_unit(&st);
+        // PRNG draw (sample.c:173): one step per stochastic row
+        st_rng = a.rng[row];
+        const double u = rng_unit(&st_rng);
 
-            bool done = false;
-            const int n = s.cnt;
-            if (collect && n <= CAP && n > 0) {
-                const float lo = fmaxf(__fadd_rn(R.M, cmargin), R.thr);
-                int mine = 0;
-                for (int i = tid; i < n; i += THREADS) {
-                    const uint64_t e = buf[i];
+        bool done = false;
+        int total = 0, before = 0;
+        bool overflow = false;
+        for (int w = 0; w < CWARPS; w++) {
+            const int c = s.wcnt[w];
+            if (c < 0) overflow = true;
+            if (w < warp) before += max(c, 0);
+            total += max(c, 0);
+        }
+        if (collect && !overflow && total > 0) {
+            // keys of the survivors, compacted to [0, nk): read the warp's region
+            // into registers, then write after the barrier
+            const float lo = fmaxf(__fadd_rn(R.M, cmargin), R.thr);
+            const int mycnt = max(s.wcnt[warp], 0);
+            uint64_t key[KREG];
+            int keep_n = 0;
+#pragma unroll
+            for (int k = 0; k < KREG; k++) {
+                const int i = lane + 32 * k;
+                key[k] = 0ull;
+                if (i < mycnt) {
+                    const uint64_t e = region[i];
                     const float sc = __uint_as_float((uint32_t)(e >> 32));
-                    const uint32_t idx = (uint32_t)e;
-                    uint64_t key = 0;
                     if (sc >= lo) {
-                        const uint32_t pk = p_key(sc, R.M, R.thr, R.inv);
-                        key = ((uint64_t)pk << 32) | (uint32_t)(~idx);
-                        mine++;
+                        const uint32_t idx = (uint32_t)e;
+                        key[k] = ((uint64_t)p_key(sc, R.M, R.thr, R.inv) << 32) | (uint32_t)(~idx);
+                        keep_n++;
                     }
-                    buf[i] = key;
-                }
-                int n2 = 1;
-                while (n2 < n) n2 <<= 1;
-                for (int i = n + tid; i < n2; i += THREADS) buf[i] = 0ull;
-                const int nk = block_sum_i(mine, s);
-                if (nk > 0) {
-                    bitonic_desc(buf, n2);
-                    if (tid < 32) candidate_cuts(buf, nk, P, __fmul_rn(P.min_p, R.inv), u, s);
-                    __syncthreads();
-                    done = true;
-                    path = QUASAR_PATH_CANDIDATE;
                 }
             }
-            if (!done) {
-                __syncthreads();
-                select_path(R, bits, H, P, u, s);
-                path = QUASAR_PATH_SELECT;
+            // exclusive position of this lane's keys among all kept keys
+            const int wincl = warp_incl_scan(keep_n, lane);
+            if (lane == 31) s.ri[warp] = wincl;
+            csync();
+            int pos = wincl - keep_n;
+            int nk = 0;
+            for (int w = 0; w < CWARPS; w++) {
+                if (w < warp) pos += s.ri[w];
+                nk += s.ri[w];
             }
-            if (tid == 0) a.rng[row] = st;
+#pragma unroll
+            for (int k = 0; k < KREG; k++)
+                if (key[k] != 0ull) buf[pos++] = key[k];
+            int n2 = 1;
+            while (n2 < nk) n2 <<= 1;
+            for (int i = nk + tid; i < n2; i += CONSUMERS) buf[i] = 0ull;
+            csync();
+            if (nk > 0) {
+                bitonic_desc(buf, n2);
+                if (tid < 32) candidate_cuts(buf, nk, P, __fmul_rn(P.min_p, R.inv), u, s);
+                done = true;
+                path = QUASAR_PATH_CANDIDATE;
+            }
+            csync();
         }
+        if (!done) {
+            csync();
+            select_path(R, bits8, H, P, u, s);
+            path = QUASAR_PATH_SELECT;
+        }
+    }
 
-        // ---- epilogue: clear the bitset, record, outputs ----
-        const int chosen = s.res_id;
-        if (R.use_pen) {
-            for (int i = tid; i < len; i += THREADS) {
-                const int id = ring[(head + i) % cap];
-                if (id >= 0 && id < a.V) bits[id >> 5] = 0u;
+    // ---- epilogue: clear the bitset, record, outputs ----
+    const int chosen = *reinterpret_cast<volatile int*>(&s.abort) ? -1 : s.res_id;
+    if (R.use_pen) {
+        for (int i = tid; i < len; i += CONSUMERS) {
+            const int id = ring[(head + i) % cap];
+            if (id >= 0 && id < a.V) bits[id >> 5] = 0u;
+        }
+    }
+    csync();
+    if (tid == 0) {
+        if (P.T > 0.0f) a.rng[row] = st_rng;
+        a.out[row] = chosen;
+        if (a.diag) {
+            quasar_pick_diag d;
+            d.n_kept = s.res_nc;
+            d.p_chosen = s.res_p;
+            d.inv_sum = R.inv;
+            d.path = path;
+            a.diag[row] = d;
+        }
+        if (a.record && cap > 0 && a.hist_len && a.hist_head && chosen >= 0) {
+            int32_t* wring = a.hist + (int64_t)row * cap;
+            if (len < cap) {
+                wring[(head + len) % cap] = chosen;
+                a.hist_len[row] = len + 1;
+            } else {
+                wring[head] = chosen;
+                a.hist_head[row] = (head + 1) % cap;
             }
         }
-        __syncthreads();
-        if (tid == 0) {
-            a.out[row] = chosen;
-            if (a.diag) {
-                quasar_pick_diag d;
-                d.n_kept = s.res_nc;
-                d.p_chosen = s.res_p;
-                d.inv_sum = R.inv;
-                d.path = path;
-                a.diag[row] = d;
-            }
-            if (a.record && cap > 0 && a.hist_len && a.hist_head) {
-                int32_t* wring = a.hist + (int64_t)row * cap;
-                if (len < cap) {
-                    wring[(head + len) % cap] = chosen;
-                    a.hist_len[row] = len + 1;
-                } else {
-                    wring[head] = chosen;
-                    a.hist_head[row] = (head + 1) % cap;
+    }
+    csync();
+}
+
+// ---------------------------------------------------------------------------
+// Dynamic shared memory of the LDG kernel: [scratch][bits]; of the TMA kernel:
+// [ring NSTAGE x 16 KB][scratch][bits][full bars][empty bars].
+
+__global__ void __launch_bounds__(CONSUMERS, 3) sample_rows_ldg(RowsArgs a) {
+    extern __shared__ __align__(128) unsigned char dyn[];
+    uint64_t* buf = reinterpret_cast<uint64_t*>(dyn);
+    uint32_t* bits = reinterpret_cast<uint32_t*>(dyn + SCRATCH_BYTES);
+    __shared__ Shared s;
+    for (int i = threadIdx.x; i < a.nwords; i += CONSUMERS) bits[i] = 0u;
+    if (threadIdx.x == 0) s.abort = 0;
+    csync();
+    LdgSource src;
+    for (int row = blockIdx.x; row < a.B; row += gridDim.x) process_row(a, row, src, buf, bits, s);
+}
+
+__global__ void __launch_bounds__(CONSUMERS + 32, 2) sample_rows_tma(RowsArgs a) {
+    extern __shared__ __align__(128) unsigned char dyn[];
+    float* ring = reinterpret_cast<float*>(dyn);
+    uint64_t* buf = reinterpret_cast<uint64_t*>(dyn + NSTAGE * TILE_BYTES);
+    uint32_t* bits = reinterpret_cast<uint32_t*>(dyn + NSTAGE * TILE_BYTES + SCRATCH_BYTES);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(dyn + NSTAGE * TILE_BYTES + SCRATCH_BYTES +
+                                                 ((a.nwords * 4 + 7) & ~7));
+    __shared__ Shared s;
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + NSTAGE);
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NSTAGE; i++) {
+            mbar_init(full0 + 8u * i, 1);            // producer's arrive.expect_tx
+            mbar_init(empty0 + 8u * i, CWARPS);     // one arrival per consumer warp
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        s.abort = 0;
+    }
+    for (int i = threadIdx.x; i < a.nwords; i += blockDim.x) bits[i] = 0u;
+    __syncthreads();
+
+    if (threadIdx.x >= CONSUMERS) {
+        // ---- producer warp: lane 0 streams every chunk of this CTA's rows ----
+        if (threadIdx.x != CONSUMERS) return;
+        const int ntiles = ((a.V + 7) / 8 + OCT_TILE - 1) / OCT_TILE;
+        const int64_t row_bytes = (int64_t)a.V * 4;
+        uint32_t g = 0;
+        for (int row = blockIdx.x; row < a.B; row += gridDim.x) {
+            const char* src = reinterpret_cast<const char*>(a.logits + (int64_t)row * a.ld);
+            for (int c = 0; c < ntiles; c++, g++) {
+                const int st = (int)(g % NSTAGE);
+                if (g >= (uint32_t)NSTAGE) {
+                    const uint32_t par = ((g / NSTAGE) - 1u) & 1u;
+                    if (!mbar_wait(empty0 + 8u * st, par)) {
+                        s.abort = 1;
+                        return;  // consumers time out on the missing chunk and finish
+                    }
                 }
+                const int64_t off = (int64_t)c * TILE_BYTES;
+                const uint32_t bytes = (uint32_t)min((int64_t)TILE_BYTES, row_bytes - off);
+                mbar_arrive_tx(full0 + 8u * st, bytes);
+                bulk_g2s(smem_u32(ring + st * TILE_ELEMS), src + off, bytes, full0 + 8u * st);
             }
         }
-        __syncthreads();
+        return;
+    }
+    TmaSource src;
+    src.ring = ring;
+    src.full0 = full0;
+    src.empty0 = empty0;
+    src.g = 0;
+    for (int row = blockIdx.x; row < a.B; row += gridDim.x) process_row(a, row, src, buf, bits, s);
+    // After an abort, give chunks still in flight a bounded chance to land
+    // before the CTA (and its shared memory) goes away.
+    if (threadIdx.x == 0 && *reinterpret_cast<volatile int*>(&s.abort)) {
+        for (int k = 1; k <= NSTAGE && (uint32_t)k <= src.g; k++) {
+            const uint32_t g = src.g - k;
+            mbar_wait(full0 + 8u * (g % NSTAGE), (g / NSTAGE) & 1u);
+        }
     }
 }
 
 }  // namespace rows
 
-size_t rows_smem_bytes(int V) {
-    const int nwords = ((V + 31) >> 5) + 1;
-    return (size_t)rows::CAP * sizeof(uint64_t) + (size_t)nwords * sizeof(uint32_t);
+static int nwords_for(int V) { return ((V + 31) >> 5) + 1; }
+
+size_t rows_smem_bytes(int V) {  // LDG kernel
+    return (size_t)rows::SCRATCH_BYTES + (size_t)nwords_for(V) * sizeof(uint32_t);
 }
 
-int rows_threads() { return rows::THREADS; }
+size_t rows_tma_smem_bytes(int V) {
+    return (size_t)rows::NSTAGE * rows::TILE_BYTES + rows::SCRATCH_BYTES +
+           (((size_t)nwords_for(V) * 4 + 7) & ~(size_t)7) + 2 * rows::NSTAGE * sizeof(uint64_t);
+}
+
+int rows_threads() { return rows::CONSUMERS; }
+
+namespace {
+struct KernelCfg {
+    size_t smem_set[64];
+    int persistent[64];  // resident CTAs per device for the TMA kernel
+};
+thread_local KernelCfg g_ldg = {}, g_tma = {};
+}  // namespace
 
 cudaError_t launch_sample_rows(const RowsArgs& args, int grid, cudaStream_t stream) {
-    const size_t smem = rows_smem_bytes(args.V);
-    static thread_local size_t configured[64] = {0};
+    RowsArgs a = args;
+    a.nwords = nwords_for(args.V);
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
     if (err != cudaSuccess) return err;
-    if (dev >= 0 && dev < 64 && configured[dev] < smem) {
-        err = cudaFuncSetAttribute(rows::sample_rows_kernel,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (err != cudaSuccess) return err;
-        configured[dev] = smem;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (a.tma) {
+        const size_t smem = rows_tma_smem_bytes(a.V);
+        if (g_tma.smem_set[dev] < smem) {
+            err = cudaFuncSetAttribute(rows::sample_rows_tma, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+            if (err != cudaSuccess) return err;
+            g_tma.smem_set[dev] = smem;
+            g_tma.persistent[dev] = 0;
+        }
+        if (g_tma.persistent[dev] == 0) {
+            int per_sm = 0, sms = 0;
+            err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rows::sample_rows_tma,
+                                                                rows::CONSUMERS + 32, smem);
+            if (err != cudaSuccess) return err;
+            err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+            if (err != cudaSuccess) return err;
+            g_tma.persistent[dev] = max(1, per_sm) * sms;
+        }
+        const int g = min(grid, g_tma.persistent[dev]);
+        rows::sample_rows_tma<<<g, rows::CONSUMERS + 32, smem, stream>>>(a);
+    } else {
+        const size_t smem = rows_smem_bytes(a.V);
+        if (g_ldg.smem_set[dev] < smem) {
+            err = cudaFuncSetAttribute(rows::sample_rows_ldg, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+            if (err != cudaSuccess) return err;
+            g_ldg.smem_set[dev] = smem;
+        }
+        rows::sample_rows_ldg<<<grid, rows::CONSUMERS, smem, stream>>>(a);
     }
-    RowsArgs a = args;
-    a.nwords = ((args.V + 31) >> 5) + 1;
-    rows::sample_rows_kernel<<<grid, rows::THREADS, smem, stream>>>(a);
     return cudaGetLastError();
 }
 

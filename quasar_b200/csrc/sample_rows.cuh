@@ -24,11 +24,13 @@ struct RowsArgs {
     int32_t* out;
     quasar_pick_diag* diag;
     int flags;
-    int vec;     // rows 16-byte aligned with ld % 4 == 0
+    int vec;     // rows 32-byte aligned with ld % 8 == 0 (256-bit global loads)
+    int tma;     // rows 16-byte aligned, ld % 4 == 0, V % 4 == 0 (bulk-copy ring kernel)
     int nwords;  // bitset words (set by the launcher)
 };
 
-size_t rows_smem_bytes(int V);
+size_t rows_smem_bytes(int V);      // one-CTA-per-row kernel
+size_t rows_tma_smem_bytes(int V);  // persistent bulk-copy ring kernel
 int rows_threads();
 cudaError_t launch_sample_rows(const RowsArgs& args, int grid, cudaStream_t stream);
 

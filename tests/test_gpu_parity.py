@@ -237,3 +237,40 @@ def test_dropin_sequence_matches_reference():
         got = [s.pick(steps[t]) for t in range(n)]
         s.close()
         assert got == list(ref_ids), (got, list(ref_ids))
+
+
+@pytest.mark.parametrize("prm_kw", [dict(temperature=0.0, repeat_penalty=1.3),
+                                    dict(temperature=1.1, top_p=0.95, min_p=0.05, repeat_penalty=1.1),
+                                    dict(temperature=0.7, top_k=20, top_p=0.8)])
+def test_ring_kernel_equals_row_kernel(prm_kw):
+    """The bulk-copy ring kernel and the one-CTA-per-row kernel give identical
+    rows (ids, kept counts, p bits, PRNG), on the same seeded inputs."""
+    B = 300
+    logits, hist = gpu_inputs(O.SYNTH_NORMAL, 21, B, V_FULL, 3.0, H=128, hist_seed=22)
+    prm = O.make_params(1, **prm_kw)
+    seeds = _seeds(B, 808)
+    a = run_gpu(logits, prm, seeds, hist=hist)
+    b = run_gpu(logits, prm, seeds, hist=hist, flags=2)
+    assert np.array_equal(a[0], b[0])
+    assert np.array_equal(a[1]["n_kept"], b[1]["n_kept"])
+    assert np.array_equal(a[1]["p_chosen"].view(np.uint32), b[1]["p_chosen"].view(np.uint32))
+    assert np.array_equal(a[2], b[2])
+
+
+@pytest.mark.parametrize("offset,extra", [(1, 0), (4, 3), (0, 5)])
+def test_strided_and_unaligned_rows(offset, extra):
+    """Row stride ld > V and a base pointer off the 16/32-byte grid take the
+    scalar-load path and still match the oracle."""
+    import torch
+    B, V = 24, 20000
+    ld = V + extra
+    src, _ = gpu_inputs(O.SYNTH_NORMAL, 55, B, V, 2.5)
+    store = torch.full((B * ld + offset + 8,), float("nan"), dtype=torch.float32, device="cuda")
+    view = store[offset:offset + B * ld].view(B, ld)
+    view[:, :V] = src
+    logits = view[:, :V]
+    prm = O.make_params(1, temperature=0.9, min_p=0.03, top_p=0.9)
+    seeds = _seeds(B, 64)
+    ids, diag, rng = run_gpu(logits, prm, seeds)
+    res, rng_ref = run_oracle(src, prm, seeds)
+    assert_parity(ids, diag, rng, res, rng_ref)
