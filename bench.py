@@ -231,7 +231,7 @@ def run_ours(args) -> None:
 
     def step(src=logits):
         q.pick_batch(src, rng, d_params=d_params, hist=hist, hist_len=hist_len,
-                     hist_head=hist_head, record=True, out=out, stream=stream)
+                     hist_head=hist_head, record=True, out=out, flags=args.flags, stream=stream)
 
     def barrier():
         if world > 1:
@@ -329,6 +329,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--rows", type=int, default=B, help="rows per GPU (profiling runs use fewer)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg (profiling)")
+    ap.add_argument("--flags", type=int, default=0, help="quasar_sampler_pick_batch flags (A/B runs)")
     args = ap.parse_args()
     globals()["B"] = args.rows
     if args.impl == "reference":

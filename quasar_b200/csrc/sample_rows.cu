@@ -6,16 +6,19 @@
 //   1. history ring -> shared-memory bitset of penalized ids (sample.c:120)
 //   2. ONE pass over the row from HBM: penalty (sample.c:124), temperature scale
 //      (sample.c:137,142), running max, online window sum of exp(sc - running
-//      max) in double (sample.c:147), and - when min_p > 0 - collection of every
-//      element that can survive the min-p cut into warp-private candidate lists.
-//      Elements more than 30 below the running max contribute < e^-30 each to
-//      that sum instead of being dropped (relative effect < V*e^-30 in the worst
-//      case, ~1e-11 on realistic rows).
-//   3. candidate path: exact p = (float)exp(sc - max) * (float)(1/sum) for the
-//      candidates, bitonic sort by (p desc, id asc) (= glibc's stable qsort of
-//      sample.c:151), top-k / top-p / min-p cuts and the inverse-CDF draw with
-//      the row's xorshift64* state (sample.c:153-177).
-//   4. select path (any parameters, or when the candidate lists overflow): an
+//      max) in double (sample.c:147), and a 16-bit upper bound of each
+//      thread-tile's max (16 elements) kept in shared memory. Elements more than
+//      30 below the running max contribute < e^-30 each to that sum instead of
+//      being dropped (relative effect < V*e^-30 in the worst case, ~1e-11 on
+//      realistic rows).
+//   3. candidate path (min_p > 0 or top_k <= 256): with the row max known, the
+//      kept prefix lies above a threshold (min-p floor, or the k-th largest tile
+//      max); only thread-tiles whose max clears it are read again (a few % of
+//      the row). Their survivors get exact p = (float)exp(sc - max) *
+//      (float)(1/sum), a bitonic sort by (p desc, id asc) (= glibc's stable
+//      qsort of sample.c:151), then the top-k / top-p / min-p cuts and the
+//      inverse-CDF draw with the row's xorshift64* state (sample.c:153-177).
+//   4. select path (any parameters, or when the candidates exceed 2048): an
 //      exact radix select over the p keys of the whole row, re-reading it.
 // Greedy rows (temperature <= 0) take one pass: penalized argmax, first index
 // on ties, no PRNG step (sample.c:130-134).
@@ -23,7 +26,7 @@
 // Two kernels share the per-row code:
 //   sample_rows_tma  persistent CTAs of 8 consumer warps + 1 producer warp. The
 //                    producer streams the rows' 16 KB chunks with cp.async.bulk
-//                    (TMA, no multicast) into a 4-stage shared-memory ring
+//                    (TMA, no multicast) into a 3-stage shared-memory ring
 //                    guarded by mbarriers, running ahead into the next row
 //                    while the consumers finish the current one. Needs rows
 //                    that start 16-byte aligned and V % 4 == 0.
@@ -44,10 +47,11 @@ constexpr int CWARPS = CONSUMERS / 32;
 constexpr int OCT_TILE = 2 * CONSUMERS;        // 32-byte octets per tile
 constexpr int TILE_ELEMS = 8 * OCT_TILE;       // 4096 elements per tile / chunk
 constexpr int TILE_BYTES = 4 * TILE_ELEMS;     // 16 KB
-constexpr int NSTAGE = 4;                      // ring depth of the TMA kernel
+constexpr int NSTAGE = 3;                      // ring depth of the TMA kernel
 constexpr int CAP = 2048;                      // candidate entries per row
-constexpr int CAPW = CAP / CWARPS;             // per-warp region (256)
-constexpr int KREG = CAPW / 32;                // entries per lane when a region is moved
+constexpr int TMAX_TILES = 40;                 // tile-max slots per thread (groups of tiles beyond)
+constexpr int TMAX_BYTES = TMAX_TILES * CONSUMERS * 2;
+constexpr int TOPK_MAX = 256;                  // largest top_k the candidate path takes
 constexpr int NB = 1024;                       // radix bins per level (10 bits)
 constexpr long long WAIT_CYCLES = 1ll << 32;   // ~2 s: bound on any mbarrier wait
 
@@ -59,12 +63,14 @@ struct Hist {
     unsigned long long mass2[NB];
     int32_t minid2[NB];
 };
-constexpr int SCRATCH_BYTES = sizeof(Hist) > CAP * 8 ? (int)sizeof(Hist) : CAP * 8;
+// candidate keys [CAP] followed by the tile-max table; the select path's
+// histograms alias both
+constexpr int SCRATCH_BYTES =
+    (int)sizeof(Hist) > CAP * 8 + TMAX_BYTES ? (int)sizeof(Hist) : CAP * 8 + TMAX_BYTES;
 
 struct Shared {
-    unsigned int maxkey;  // ord_key of the largest scaled logit published so far
     int abort;            // a bounded wait gave up
-    int wcnt[CWARPS];     // candidates per warp region (-1: overflow)
+    int ncand;            // candidate keys appended
     float rf[CWARPS];
     double rd[CWARPS];
     int ri[CWARPS];
@@ -560,27 +566,68 @@ __device__ void candidate_cuts(const uint64_t* keys, int nk, const RowParams& P,
     }
 }
 
-// Drops the entries of a warp's candidate region whose scaled logit is below
-// tau; returns the new count (warp-uniform).
-__device__ int warp_prune(uint64_t* region, int cnt, float tau, int lane) {
-    uint64_t e[KREG];
-#pragma unroll
-    for (int k = 0; k < KREG; k++) {
-        const int i = lane + 32 * k;
-        e[k] = i < cnt ? region[i] : 0ull;
+// 16-bit prefix of the order-preserving key, rounded up: an upper bound of f
+// that stays monotone (tile maxima table).
+__device__ __forceinline__ uint16_t key16_up(float f) {
+    const uint32_t k = ord_key(f);
+    return (uint16_t)min((k >> 16) + ((k & 0xFFFFu) ? 1u : 0u), 0xFFFFu);
+}
+
+// Warp 0: first of 256 count bins, from the top down, where the running count
+// reaches target (>= 1). Publishes bin (-1: not reached) and the count above.
+__device__ void find_bin256(const uint32_t* h, uint32_t target, Shared& s) {
+    csync();
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        const int hi = 255 - 8 * lane;
+        uint32_t t = 0;
+        for (int b = hi; b > hi - 8; b--) t += h[b];
+        const uint32_t incl = warp_incl_scan(t, lane);
+        const unsigned bal = __ballot_sync(FULL, incl >= target);
+        if (bal == 0u) {
+            if (lane == 0) s.bin = -1;
+        } else if (lane == __ffs(bal) - 1) {
+            uint32_t acc = incl - t;
+            int found = hi - 7;
+            for (int b = hi; b > hi - 8; b--) {
+                if (acc + h[b] >= target) {
+                    found = b;
+                    break;
+                }
+                acc += h[b];
+            }
+            s.bin = found;
+            s.bin_cnt_above = acc;
+        }
     }
-    __syncwarp();
-    int out = 0;
-#pragma unroll
-    for (int k = 0; k < KREG; k++) {
-        const int i = lane + 32 * k;
-        const bool keep = i < cnt && __uint_as_float((uint32_t)(e[k] >> 32)) >= tau;
-        const unsigned bal = __ballot_sync(FULL, keep);
-        if (keep) region[out + __popc(bal & ((1u << lane) - 1u))] = e[k];
-        out += __popc(bal);
-    }
-    __syncwarp();
-    return out;
+    csync();
+}
+
+// Lower bound of the k-th largest scaled logit of the row from the tile-max
+// table: the k-th largest of nslot 16-bit upper-bound keys, mapped back below
+// its 16-bit bucket and lowered by a margin that covers ties in p.
+__device__ float topk_floor(const uint16_t* tmax, int nslot, int k, uint64_t* scratch, Shared& s) {
+    uint32_t* h = reinterpret_cast<uint32_t*>(scratch);
+    for (int i = threadIdx.x; i < 256; i += CONSUMERS) h[i] = 0u;
+    csync();
+    for (int i = threadIdx.x; i < nslot; i += CONSUMERS) atomicAdd(&h[tmax[i] >> 8], 1u);
+    find_bin256(h, (uint32_t)k, s);
+    const int hb = s.bin;
+    if (hb < 0) return -INFINITY;
+    const uint32_t above = s.bin_cnt_above;
+    csync();
+    for (int i = threadIdx.x; i < 256; i += CONSUMERS) h[i] = 0u;
+    csync();
+    for (int i = threadIdx.x; i < nslot; i += CONSUMERS)
+        if ((tmax[i] >> 8) == hb) atomicAdd(&h[tmax[i] & 255], 1u);
+    find_bin256(h, (uint32_t)k - above, s);
+    const int lb = s.bin;
+    csync();
+    if (lb < 0) return -INFINITY;
+    const uint32_t key = ((uint32_t)hb << 8) | (uint32_t)lb;
+    if (key == 0u) return -INFINITY;
+    const float t = ord_key_inv((key - 1u) << 16);
+    return t - (1e-5f + 1e-5f * fabsf(t));
 }
 
 // ---------------------------------------------------------------------------
@@ -677,7 +724,6 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
             if (id >= 0 && id < a.V) atomicOr(&bits[id >> 5], 1u << (id & 31));
         }
     }
-    if (tid == 0) s.maxkey = 0u;
     csync();
     src.begin(R);
 
@@ -739,13 +785,12 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
         path = QUASAR_PATH_GREEDY;
         csync();
     } else {
-        // ---- one streaming pass: max, online window sum, candidates ----
+        // ---- one streaming pass: max, online window sum, tile maxima ----
         R.inv_t = __fdiv_rn(1.0f, P.T);
-        const bool collect = !(a.flags & QUASAR_FLAG_EXACT_SELECT) && P.min_p > 0.0f;
-        // every element with p >= min_p * p_max has sc >= max + cmargin (1% slack)
-        const float cmargin = collect ? (float)(log((double)fminf(P.min_p, 1.0f)) - 0.01) : 0.0f;
-        uint64_t* region = buf + warp * CAPW;
-        int wcnt = 0;  // warp-uniform; -1 after an overflow
+        // slots of the tile-max table: one per thread and group of g tiles
+        const int g = (R.ntiles + TMAX_TILES - 1) / TMAX_TILES;
+        uint16_t* tmax = reinterpret_cast<uint16_t*>(reinterpret_cast<unsigned char*>(buf) + CAP * 8);
+        float slotmax = -INFINITY;
         float m = -INFINITY;
         double S = 0.0;
         for (int it = 0; it < R.ntiles; it++) {
@@ -772,9 +817,7 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
             if (mt > m) {
                 S *= exp((double)m - (double)mt);
                 m = mt;
-                if (collect) atomicMax(&s.maxkey, ord_key(m));
             }
-            if (it == 0) csync();  // first-tile maxima are published
             if (m > -INFINITY) {
                 // sample.c:148 against the running max
                 float e[16];
@@ -786,43 +829,13 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
                     for (int j = 0; j < w; j++) e[j] += e[j + w];
                 S += (double)e[0];
             }
-            if (collect) {
-                const unsigned int mk = *reinterpret_cast<volatile unsigned int*>(&s.maxkey);
-                const float ref = mk ? fmaxf(m, ord_key_inv(mk)) : m;
-                const float tau = __fadd_rn(ref, cmargin);
-                uint32_t mask = 0u;
-                if (mt >= tau) {
-#pragma unroll
-                    for (int j = 0; j < 16; j++) mask |= (sc[j] >= tau ? 1u : 0u) << j;
-                }
-                if (__ballot_sync(FULL, mask != 0u) && wcnt >= 0) {
-                    // warp-private append: no shared atomics on the streaming path
-                    const int cnt = __popc(mask);
-                    const int incl = warp_incl_scan(cnt, lane);
-                    const int total = __shfl_sync(FULL, incl, 31);
-                    if (wcnt + total > CAPW) wcnt = warp_prune(region, wcnt, tau, lane);
-                    if (wcnt + total > CAPW) {
-                        wcnt = -1;  // overflow: this row takes the select path
-                    } else {
-                        int pos = wcnt + incl - cnt;
-                        if (mask) {
-#pragma unroll
-                            for (int j = 0; j < 16; j++) {
-                                if (mask & (1u << j)) {
-                                    const int idx = j < 8 ? 8 * o0 + j : 8 * o1 + (j - 8);
-                                    region[pos] = idx < R.V
-                                                      ? ((uint64_t)__float_as_uint(sc[j]) << 32) | (uint32_t)idx
-                                                      : ((uint64_t)0xFF800000u << 32);
-                                    pos++;
-                                }
-                            }
-                        }
-                        wcnt += total;
-                    }
-                }
+            // upper bound of this thread's max over the slot's tiles (16-bit key)
+            slotmax = fmaxf(slotmax, mt);
+            if (it % g == g - 1 || it == R.ntiles - 1) {
+                tmax[(it / g) * CONSUMERS + tid] = key16_up(slotmax);
+                slotmax = -INFINITY;
             }
         }
-        if (lane == 0) s.wcnt[warp] = wcnt;
         R.M = block_max_f(m, s);
         const double contrib = (m > -INFINITY) ? S * exp((double)m - (double)R.M) : 0.0;
         const double Stot = block_sum_d(contrib, s);
@@ -834,55 +847,54 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
         const double u = rng_unit(&st_rng);
 
         bool done = false;
-        int total = 0, before = 0;
-        bool overflow = false;
-        for (int w = 0; w < CWARPS; w++) {
-            const int c = s.wcnt[w];
-            if (c < 0) overflow = true;
-            if (w < warp) before += max(c, 0);
-            total += max(c, 0);
-        }
-        if (collect && !overflow && total > 0) {
-            // keys of the survivors, compacted to [0, nk): read the warp's region
-            // into registers, then write after the barrier
-            const float lo = fmaxf(__fadd_rn(R.M, cmargin), R.thr);
-            const int mycnt = max(s.wcnt[warp], 0);
-            uint64_t key[KREG];
-            int keep_n = 0;
+        // Candidate path. The kept prefix lies above a threshold that is known
+        // once M and the tile maxima are: min_p -> sc >= M + ln(min_p) - 0.01
+        // (every p >= min_p * p_max clears it); top_k -> the k-th largest tile
+        // max, less a margin for p ties (k distinct elements reach it). Only the
+        // thread-tiles whose max clears the threshold are read again.
+        const bool by_minp = P.min_p > 0.0f;
+        const bool by_topk = P.top_k > 0 && P.top_k <= TOPK_MAX;
+        if (!(a.flags & QUASAR_FLAG_EXACT_SELECT) && (by_minp || by_topk)) {
+            const int nslot = ((R.ntiles + g - 1) / g) * CONSUMERS;
+            float tau = -INFINITY;
+            if (by_minp) tau = __fadd_rn(R.M, (float)(log((double)fminf(P.min_p, 1.0f)) - 0.01));
+            if (by_topk) tau = fmaxf(tau, topk_floor(tmax, nslot, P.top_k, buf, s));
+            const float lo = fmaxf(tau, R.thr);
+            const uint32_t kt = ord_key(lo) >> 16;
+            if (tid == 0) s.ncand = 0;
+            csync();
+            for (int sl = 0; sl * CONSUMERS < nslot; sl++) {
+                if (tmax[sl * CONSUMERS + tid] < kt) continue;
+                for (int it = sl * g; it < min((sl + 1) * g, R.ntiles); it++) {
+                    float v[16];
+                    LdgSource::load(R, it, v);
+                    const int o0 = it * OCT_TILE + tid, o1 = o0 + CONSUMERS;
+                    if (R.use_pen) {
+                        apply_pen_oct(v, o0 < R.noct ? bits8[o0] : 0u, R.rp);
+                        apply_pen_oct(v + 8, o1 < R.noct ? bits8[o1] : 0u, R.rp);
+                    }
 #pragma unroll
-            for (int k = 0; k < KREG; k++) {
-                const int i = lane + 32 * k;
-                key[k] = 0ull;
-                if (i < mycnt) {
-                    const uint64_t e = region[i];
-                    const float sc = __uint_as_float((uint32_t)(e >> 32));
-                    if (sc >= lo) {
-                        const uint32_t idx = (uint32_t)e;
-                        key[k] = ((uint64_t)p_key(sc, R.M, R.thr, R.inv) << 32) | (uint32_t)(~idx);
-                        keep_n++;
+                    for (int j = 0; j < 16; j++) {
+                        const float sc = __fmul_rn(v[j], R.inv_t);
+                        const int idx = j < 8 ? 8 * o0 + j : 8 * o1 + (j - 8);
+                        if (sc >= lo && idx < R.V) {
+                            const int pos = atomicAdd(&s.ncand, 1);
+                            if (pos < CAP)
+                                buf[pos] = ((uint64_t)p_key(sc, R.M, R.thr, R.inv) << 32) |
+                                           (uint32_t)(~(uint32_t)idx);
+                        }
                     }
                 }
             }
-            // exclusive position of this lane's keys among all kept keys
-            const int wincl = warp_incl_scan(keep_n, lane);
-            if (lane == 31) s.ri[warp] = wincl;
             csync();
-            int pos = wincl - keep_n;
-            int nk = 0;
-            for (int w = 0; w < CWARPS; w++) {
-                if (w < warp) pos += s.ri[w];
-                nk += s.ri[w];
-            }
-#pragma unroll
-            for (int k = 0; k < KREG; k++)
-                if (key[k] != 0ull) buf[pos++] = key[k];
-            int n2 = 1;
-            while (n2 < nk) n2 <<= 1;
-            for (int i = nk + tid; i < n2; i += CONSUMERS) buf[i] = 0ull;
-            csync();
-            if (nk > 0) {
+            const int nk = s.ncand;
+            if (nk > 0 && nk <= CAP) {
+                int n2 = 1;
+                while (n2 < nk) n2 <<= 1;
+                for (int i = nk + tid; i < n2; i += CONSUMERS) buf[i] = 0ull;
+                csync();
                 bitonic_desc(buf, n2);
-                if (tid < 32) candidate_cuts(buf, nk, P, __fmul_rn(P.min_p, R.inv), u, s);
+                if (tid < 32) candidate_cuts(buf, nk, P, by_minp ? __fmul_rn(P.min_p, R.inv) : 0.0f, u, s);
                 done = true;
                 path = QUASAR_PATH_CANDIDATE;
             }
