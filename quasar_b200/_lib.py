@@ -40,6 +40,7 @@ SIGNATURES = {
     "quasar_synth_logits": ([_I, _U64, _I64, _I, _I, _I64, _F, _P, _P], _I),
     "quasar_synth_hist": ([_U64, _I64, _I, _I, _I, _P, _P], _I),
     "quasar_synth_uniform": ([_U64, _I64, _I, _F, _F, _P, _P], _I),
+    "quasar_selftest_exp": ([_P, _P, _I, _I, _P], _I),
 }
 
 _lib: ctypes.CDLL | None = None

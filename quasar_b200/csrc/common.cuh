@@ -51,6 +51,25 @@ __device__ __forceinline__ RowParams clamp_params(const quasar_sample_params& p)
     return r;
 }
 
+// e^x for x <= 0, used for the terms of the window sum only (the reported
+// probabilities use a correctly rounded exp). exp(x) = 2^(x*log2e): the product
+// x*log2e is split into t + tl exactly (FMA remainder, plus the rounding error
+// of the float log2e), 2^t comes from ex2.approx and the remainder is applied
+// as 2^t * (1 + tl*ln2). The error is that of ex2.approx alone (~2 ulp, checked
+// for size and bias against a double-precision exp by the GPU self-test).
+// x < -126 returns 0 (flushed), so x = -inf is safe.
+__device__ __forceinline__ float exp_term(float x) {
+    const float kLog2e = 1.44269502162933349609375f;    // float(log2 e)
+    const float kLog2eLo = 1.925963033500011e-08f;       // log2 e - kLog2e
+    x = fmaxf(x, -126.0f);
+    const float t = __fmul_rn(x, kLog2e);
+    float tl = __fmaf_rn(x, kLog2e, -t);
+    tl = __fmaf_rn(x, kLog2eLo, tl);
+    float e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(t));
+    return __fmaf_rn(e, __fmul_rn(tl, 0.693147182464599609375f), e);
+}
+
 template <typename T>
 __device__ __forceinline__ T warp_max(T v) {
 #pragma unroll

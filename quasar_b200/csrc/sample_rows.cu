@@ -52,6 +52,7 @@ constexpr int CAP = 2048;                      // candidate entries per row
 constexpr int TMAX_TILES = 40;                 // tile-max slots per thread (groups of tiles beyond)
 constexpr int TMAX_BYTES = TMAX_TILES * CONSUMERS * 2;
 constexpr int TOPK_MAX = 256;                  // largest top_k the candidate path takes
+constexpr int QMAX = 1024;                     // qualifying thread-tiles re-read per row
 constexpr int NB = 1024;                       // radix bins per level (10 bits)
 constexpr long long WAIT_CYCLES = 1ll << 32;   // ~2 s: bound on any mbarrier wait
 
@@ -71,6 +72,7 @@ constexpr int SCRATCH_BYTES =
 struct Shared {
     int abort;            // a bounded wait gave up
     int ncand;            // candidate keys appended
+    int nq;               // qualifying thread-tiles listed
     float rf[CWARPS];
     double rd[CWARPS];
     int ri[CWARPS];
@@ -677,10 +679,12 @@ struct TmaSource {
             v[8] = c.x; v[9] = c.y; v[10] = c.z; v[11] = c.w;
             v[12] = d.x; v[13] = d.y; v[14] = d.z; v[15] = d.w;
         }
+        if (!ok || it == R.ntiles - 1) {  // only the last chunk of a row is partial
 #pragma unroll
-        for (int k = 0; k < 8; k++) {
-            if (!ok || e0 + k >= R.V) v[k] = -INFINITY;
-            if (!ok || e1 + k >= R.V) v[8 + k] = -INFINITY;
+            for (int k = 0; k < 8; k++) {
+                if (!ok || e0 + k >= R.V) v[k] = -INFINITY;
+                if (!ok || e1 + k >= R.V) v[8 + k] = -INFINITY;
+            }
         }
     }
     __device__ __forceinline__ void release() {
@@ -822,7 +826,7 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
                 // sample.c:148 against the running max
                 float e[16];
 #pragma unroll
-                for (int j = 0; j < 16; j++) e[j] = expf(__fsub_rn(sc[j], m));
+                for (int j = 0; j < 16; j++) e[j] = exp_term(__fsub_rn(sc[j], m));
 #pragma unroll
                 for (int w = 8; w > 0; w >>= 1)
 #pragma unroll
@@ -861,33 +865,59 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
             if (by_topk) tau = fmaxf(tau, topk_floor(tmax, nslot, P.top_k, buf, s));
             const float lo = fmaxf(tau, R.thr);
             const uint32_t kt = ord_key(lo) >> 16;
-            if (tid == 0) s.ncand = 0;
+            if (tid == 0) {
+                s.ncand = 0;
+                s.nq = 0;
+            }
             csync();
+            // The qualifying thread-tiles go to a shared list first, so the
+            // re-reads spread over all threads and issue in one round.
+            uint32_t* qlist = reinterpret_cast<uint32_t*>(buf + CAP / 2);
             for (int sl = 0; sl * CONSUMERS < nslot; sl++) {
-                if (tmax[sl * CONSUMERS + tid] < kt) continue;
-                for (int it = sl * g; it < min((sl + 1) * g, R.ntiles); it++) {
-                    float v[16];
-                    LdgSource::load(R, it, v);
-                    const int o0 = it * OCT_TILE + tid, o1 = o0 + CONSUMERS;
-                    if (R.use_pen) {
-                        apply_pen_oct(v, o0 < R.noct ? bits8[o0] : 0u, R.rp);
-                        apply_pen_oct(v + 8, o1 < R.noct ? bits8[o1] : 0u, R.rp);
-                    }
+                if (tmax[sl * CONSUMERS + tid] >= kt) {
+                    const int q = atomicAdd(&s.nq, 1);
+                    if (q < QMAX) qlist[q] = (uint32_t)(sl * CONSUMERS + tid);
+                }
+            }
+            csync();
+            const int nq_all = s.nq;
+            uint32_t mine[QMAX / CONSUMERS];
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        const float sc = __fmul_rn(v[j], R.inv_t);
-                        const int idx = j < 8 ? 8 * o0 + j : 8 * o1 + (j - 8);
-                        if (sc >= lo && idx < R.V) {
-                            const int pos = atomicAdd(&s.ncand, 1);
-                            if (pos < CAP)
-                                buf[pos] = ((uint64_t)p_key(sc, R.M, R.thr, R.inv) << 32) |
-                                           (uint32_t)(~(uint32_t)idx);
+            for (int k = 0; k < QMAX / CONSUMERS; k++) {
+                const int i = k * CONSUMERS + tid;
+                mine[k] = i < min(nq_all, QMAX) ? qlist[i] : 0xFFFFFFFFu;
+            }
+            csync();  // the list is in registers before candidates overwrite it
+            if (nq_all <= QMAX) {
+#pragma unroll
+                for (int k = 0; k < QMAX / CONSUMERS; k++) {
+                    if (mine[k] == 0xFFFFFFFFu) continue;
+                    const int sl = (int)(mine[k] / CONSUMERS), owner = (int)(mine[k] % CONSUMERS);
+                    for (int it = sl * g; it < min((sl + 1) * g, R.ntiles); it++) {
+                        float v[16];
+                        const int o0 = it * OCT_TILE + owner, o1 = o0 + CONSUMERS;
+                        load_oct(R.ptr, o0, R.V, R.vec, v);
+                        load_oct(R.ptr, o1, R.V, R.vec, v + 8);
+                        if (R.use_pen) {
+                            apply_pen_oct(v, o0 < R.noct ? bits8[o0] : 0u, R.rp);
+                            apply_pen_oct(v + 8, o1 < R.noct ? bits8[o1] : 0u, R.rp);
+                        }
+#pragma unroll
+                        for (int j = 0; j < 16; j++) {
+                            const float sc = __fmul_rn(v[j], R.inv_t);
+                            const int idx = j < 8 ? 8 * o0 + j : 8 * o1 + (j - 8);
+                            if (sc >= lo && idx < R.V) {
+                                const int pos = atomicAdd(&s.ncand, 1);
+                                if (pos < CAP)
+                                    buf[pos] = ((uint64_t)p_key(sc, R.M, R.thr, R.inv) << 32) |
+                                               (uint32_t)(~(uint32_t)idx);
+                            }
                         }
                     }
                 }
             }
             csync();
-            const int nk = s.ncand;
+            const int nk = nq_all <= QMAX ? s.ncand : CAP + 1;
             if (nk > 0 && nk <= CAP) {
                 int n2 = 1;
                 while (n2 < nk) n2 <<= 1;
