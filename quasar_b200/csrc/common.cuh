@@ -70,6 +70,45 @@ __device__ __forceinline__ float exp_term(float x) {
     return __fmaf_rn(e, __fmul_rn(tl, 0.693147182464599609375f), e);
 }
 
+// e^x for x <= 0 with FMA-pipe arithmetic only: Cody-Waite reduction
+// x = k*ln2 + r (|r| <= ln2/2; ln2 split in an 11-bit head, so k*head is
+// exact, and a float tail), e^r from a degree-6 polynomial fitted to e^r on
+// [-ln2/2, ln2/2] by least squares at Chebyshev nodes (relative error 1.8e-8
+// with these float coefficients), 2^k added to the exponent field. Rounding is
+// to nearest throughout, so the error (~1 ulp) has no systematic sign.
+// x < -86 is clamped to -86 (4e-38, keeps 2^k normal).
+__device__ __forceinline__ float exp_poly(float x) {
+    const float kMagic = 12582912.0f;  // 1.5 * 2^23: adding it rounds to an integer
+    x = fmaxf(x, -86.0f);
+    const float t = __fmaf_rn(x, 1.44269502162933349609375f, kMagic);
+    const float kf = __fsub_rn(t, kMagic);
+    float r = __fmaf_rn(kf, -0.693359375f, x);               // exact
+    r = __fmaf_rn(kf, 2.1219444170128554e-04f, r);             // ln2 = head - (-tail)
+    float p = 0.0013829420786350965f;
+    p = __fmaf_rn(p, r, 0.008374771103262901f);
+    p = __fmaf_rn(p, r, 0.0416683591902256f);
+    p = __fmaf_rn(p, r, 0.1666642129421234f);
+    p = __fmaf_rn(p, r, 0.49999991059303284f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    const int k = __float_as_int(t) - __float_as_int(kMagic);
+    return __int_as_float(__float_as_int(p) + (k << 23));
+}
+
+// The exp used for the terms of the window sum (compile-time choice).
+#ifndef QS_SUM_EXP
+#define QS_SUM_EXP 2
+#endif
+__device__ __forceinline__ float sum_term_exp(float x) {
+#if QS_SUM_EXP == 0
+    return expf(x);
+#elif QS_SUM_EXP == 1
+    return exp_term(x);
+#else
+    return exp_poly(x);
+#endif
+}
+
 template <typename T>
 __device__ __forceinline__ T warp_max(T v) {
 #pragma unroll

@@ -48,11 +48,11 @@ constexpr int OCT_TILE = 2 * CONSUMERS;        // 32-byte octets per tile
 constexpr int TILE_ELEMS = 8 * OCT_TILE;       // 4096 elements per tile / chunk
 constexpr int TILE_BYTES = 4 * TILE_ELEMS;     // 16 KB
 constexpr int NSTAGE = 3;                      // ring depth of the TMA kernel
-constexpr int CAP = 2048;                      // candidate entries per row
+constexpr int CAP = 4096;                      // candidate entries per row
 constexpr int TMAX_TILES = 40;                 // tile-max slots per thread (groups of tiles beyond)
-constexpr int TMAX_BYTES = TMAX_TILES * CONSUMERS * 2;
-constexpr int TOPK_MAX = 256;                  // largest top_k the candidate path takes
-constexpr int QMAX = 1024;                     // qualifying thread-tiles re-read per row
+constexpr int TMAX_BYTES = TMAX_TILES * CONSUMERS;  // one byte per slot
+constexpr int TOPK_MAX = CONSUMERS;            // largest top_k the candidate path takes
+constexpr int QMAX = 4096;                     // qualifying thread-tiles re-read per row
 constexpr int NB = 1024;                       // radix bins per level (10 bits)
 constexpr long long WAIT_CYCLES = 1ll << 32;   // ~2 s: bound on any mbarrier wait
 
@@ -73,6 +73,7 @@ struct Shared {
     int abort;            // a bounded wait gave up
     int ncand;            // candidate keys appended
     int nq;               // qualifying thread-tiles listed
+    float tfmax[CONSUMERS];  // each consumer thread's final running max (scaled)
     float rf[CWARPS];
     double rd[CWARPS];
     int ri[CWARPS];
@@ -568,67 +569,34 @@ __device__ void candidate_cuts(const uint64_t* keys, int nk, const RowParams& P,
     }
 }
 
-// 16-bit prefix of the order-preserving key, rounded up: an upper bound of f
-// that stays monotone (tile maxima table).
-__device__ __forceinline__ uint16_t key16_up(float f) {
-    const uint32_t k = ord_key(f);
-    return (uint16_t)min((k >> 16) + ((k & 0xFFFFu) ? 1u : 0u), 0xFFFFu);
+// Tile-max table entry: how far (in 1/8 nat, rounded down, saturating at 255)
+// a slot's max lies below the thread's running max m at the slot's end. Since
+// m only grows, slot max <= (thread's final max) - d/8 holds at the end.
+__device__ __forceinline__ uint8_t tile_deficit(float m, float slotmax) {
+    const float d = __fmul_rd(__fsub_rd(m, slotmax), 8.0f);  // never above the true deficit
+    return !(d < 255.0f) ? (uint8_t)255 : (uint8_t)(int)d;   // NaN / +inf -> 255
+}
+// Upper bound of a slot's max from its entry and its thread's final max.
+__device__ __forceinline__ float tile_bound(float thread_max, uint8_t d) {
+    return __fsub_ru(thread_max, 0.125f * (float)d);
 }
 
-// Warp 0: first of 256 count bins, from the top down, where the running count
-// reaches target (>= 1). Publishes bin (-1: not reached) and the count above.
-__device__ void find_bin256(const uint32_t* h, uint32_t target, Shared& s) {
-    csync();
-    if (threadIdx.x < 32) {
-        const int lane = threadIdx.x;
-        const int hi = 255 - 8 * lane;
-        uint32_t t = 0;
-        for (int b = hi; b > hi - 8; b--) t += h[b];
-        const uint32_t incl = warp_incl_scan(t, lane);
-        const unsigned bal = __ballot_sync(FULL, incl >= target);
-        if (bal == 0u) {
-            if (lane == 0) s.bin = -1;
-        } else if (lane == __ffs(bal) - 1) {
-            uint32_t acc = incl - t;
-            int found = hi - 7;
-            for (int b = hi; b > hi - 8; b--) {
-                if (acc + h[b] >= target) {
-                    found = b;
-                    break;
-                }
-                acc += h[b];
-            }
-            s.bin = found;
-            s.bin_cnt_above = acc;
-        }
+// Lower bound of the k-th largest scaled logit of the row (k <= 256): the
+// k-th largest of the 256 per-thread maxima (256 distinct elements), lowered by
+// a margin that covers ties in p. Rank by (value desc, thread asc).
+__device__ float topk_floor(int k, Shared& s) {
+    const int tid = threadIdx.x;
+    const float mine = s.tfmax[tid];
+    int rank = 0;
+    for (int j = 0; j < CONSUMERS; j++) {
+        const float o = s.tfmax[j];
+        rank += (o > mine || (o == mine && j < tid)) ? 1 : 0;
     }
+    if (rank == k - 1) s.pf_lo = mine;
     csync();
-}
-
-// Lower bound of the k-th largest scaled logit of the row from the tile-max
-// table: the k-th largest of nslot 16-bit upper-bound keys, mapped back below
-// its 16-bit bucket and lowered by a margin that covers ties in p.
-__device__ float topk_floor(const uint16_t* tmax, int nslot, int k, uint64_t* scratch, Shared& s) {
-    uint32_t* h = reinterpret_cast<uint32_t*>(scratch);
-    for (int i = threadIdx.x; i < 256; i += CONSUMERS) h[i] = 0u;
+    const float t = s.pf_lo;
     csync();
-    for (int i = threadIdx.x; i < nslot; i += CONSUMERS) atomicAdd(&h[tmax[i] >> 8], 1u);
-    find_bin256(h, (uint32_t)k, s);
-    const int hb = s.bin;
-    if (hb < 0) return -INFINITY;
-    const uint32_t above = s.bin_cnt_above;
-    csync();
-    for (int i = threadIdx.x; i < 256; i += CONSUMERS) h[i] = 0u;
-    csync();
-    for (int i = threadIdx.x; i < nslot; i += CONSUMERS)
-        if ((tmax[i] >> 8) == hb) atomicAdd(&h[tmax[i] & 255], 1u);
-    find_bin256(h, (uint32_t)k - above, s);
-    const int lb = s.bin;
-    csync();
-    if (lb < 0) return -INFINITY;
-    const uint32_t key = ((uint32_t)hb << 8) | (uint32_t)lb;
-    if (key == 0u) return -INFINITY;
-    const float t = ord_key_inv((key - 1u) << 16);
+    if (!(t > -INFINITY)) return -INFINITY;
     return t - (1e-5f + 1e-5f * fabsf(t));
 }
 
@@ -793,7 +761,7 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
         R.inv_t = __fdiv_rn(1.0f, P.T);
         // slots of the tile-max table: one per thread and group of g tiles
         const int g = (R.ntiles + TMAX_TILES - 1) / TMAX_TILES;
-        uint16_t* tmax = reinterpret_cast<uint16_t*>(reinterpret_cast<unsigned char*>(buf) + CAP * 8);
+        uint8_t* tmax = reinterpret_cast<uint8_t*>(buf) + CAP * 8;
         float slotmax = -INFINITY;
         float m = -INFINITY;
         double S = 0.0;
@@ -826,7 +794,7 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
                 // sample.c:148 against the running max
                 float e[16];
 #pragma unroll
-                for (int j = 0; j < 16; j++) e[j] = exp_term(__fsub_rn(sc[j], m));
+                for (int j = 0; j < 16; j++) e[j] = sum_term_exp(__fsub_rn(sc[j], m));
 #pragma unroll
                 for (int w = 8; w > 0; w >>= 1)
 #pragma unroll
@@ -836,10 +804,11 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
             // upper bound of this thread's max over the slot's tiles (16-bit key)
             slotmax = fmaxf(slotmax, mt);
             if (it % g == g - 1 || it == R.ntiles - 1) {
-                tmax[(it / g) * CONSUMERS + tid] = key16_up(slotmax);
+                tmax[(it / g) * CONSUMERS + tid] = tile_deficit(m, slotmax);
                 slotmax = -INFINITY;
             }
         }
+        s.tfmax[tid] = m;
         R.M = block_max_f(m, s);
         const double contrib = (m > -INFINITY) ? S * exp((double)m - (double)R.M) : 0.0;
         const double Stot = block_sum_d(contrib, s);
@@ -862,9 +831,8 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
             const int nslot = ((R.ntiles + g - 1) / g) * CONSUMERS;
             float tau = -INFINITY;
             if (by_minp) tau = __fadd_rn(R.M, (float)(log((double)fminf(P.min_p, 1.0f)) - 0.01));
-            if (by_topk) tau = fmaxf(tau, topk_floor(tmax, nslot, P.top_k, buf, s));
+            if (by_topk) tau = fmaxf(tau, topk_floor(P.top_k, s));
             const float lo = fmaxf(tau, R.thr);
-            const uint32_t kt = ord_key(lo) >> 16;
             if (tid == 0) {
                 s.ncand = 0;
                 s.nq = 0;
@@ -874,7 +842,7 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
             // re-reads spread over all threads and issue in one round.
             uint32_t* qlist = reinterpret_cast<uint32_t*>(buf + CAP / 2);
             for (int sl = 0; sl * CONSUMERS < nslot; sl++) {
-                if (tmax[sl * CONSUMERS + tid] >= kt) {
+                if (tile_bound(m, tmax[sl * CONSUMERS + tid]) >= lo) {
                     const int q = atomicAdd(&s.nq, 1);
                     if (q < QMAX) qlist[q] = (uint32_t)(sl * CONSUMERS + tid);
                 }
