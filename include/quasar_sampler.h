@@ -94,7 +94,8 @@ typedef struct {
 
 #define QUASAR_PATH_GREEDY     0   /* temperature <= 0: penalized argmax */
 #define QUASAR_PATH_CANDIDATE  1   /* candidates collected in one HBM pass, exact cuts */
-#define QUASAR_PATH_SELECT     2   /* exact radix select over the row (any params) */
+#define QUASAR_PATH_SELECT     2   /* exact radix select over the row (any params),
+                                      in a second kernel */
 
 /* Flags for quasar_sampler_pick_batch. */
 #define QUASAR_FLAG_EXACT_SELECT  1  /* route every stochastic row through the
@@ -131,11 +132,20 @@ int quasar_sampler_pick_batch(const float *d_logits, int64_t ld, int B, int V,
                               int32_t *d_hist_len, int32_t *d_hist_head,
                               int record,
                               int32_t *d_out, quasar_pick_diag *d_diag,
+                              void *d_workspace, size_t workspace_bytes,
                               int flags, void *stream);
 
-/* Number of kernel launches one quasar_sampler_pick_batch call makes (1). A
- * row whose id comes back -1 hit the bounded-wait timeout of the bulk-copy
- * ring (a device fault, not a sampling result). */
+/* Device workspace one quasar_sampler_pick_batch call of B rows needs (the
+ * list of rows handed to the exact-select kernel). Pass d_workspace = NULL to
+ * use a workspace the library allocates per device and keeps; that one is
+ * shared, so concurrent calls on one device must each pass their own. */
+size_t quasar_sampler_workspace_bytes(int B);
+
+/* Kernel launches one quasar_sampler_pick_batch call makes (2: the streaming
+ * kernel and the exact-select kernel, which exits at once when no row needs
+ * it), plus one 4-byte memset of the workspace counter. A row whose id comes
+ * back -1 hit the bounded-wait timeout of the bulk-copy ring (a device fault,
+ * not a sampling result). */
 int quasar_sampler_pick_batch_launches(void);
 
 /* ---- synthetic inputs (benchmark / test utility, not in the reference) ---- */

@@ -10,6 +10,8 @@
 #include <string.h>
 #include <time.h>
 
+#include <mutex>
+
 #include "../../include/quasar_sampler.h"
 #include "sample_rows.cuh"
 
@@ -34,6 +36,31 @@ struct quasar_sampler {
 };
 
 namespace {
+
+// Workspace the library keeps per device for callers that pass none.
+std::mutex g_ws_mu;
+void* g_ws[64];
+size_t g_ws_bytes[64];
+
+int managed_workspace(size_t bytes, void** out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return QUASAR_ECUDA;
+    std::lock_guard<std::mutex> lock(g_ws_mu);
+    if (g_ws_bytes[dev] < bytes) {
+        if (g_ws[dev]) {
+            // a previous call may still read it
+            if (cudaDeviceSynchronize() != cudaSuccess) return QUASAR_ECUDA;
+            cudaFree(g_ws[dev]);
+            g_ws[dev] = nullptr;
+            g_ws_bytes[dev] = 0;
+        }
+        const size_t grow = bytes < ((size_t)1 << 16) ? ((size_t)1 << 16) : bytes;
+        if (cudaMalloc(&g_ws[dev], grow) != cudaSuccess) return QUASAR_ENOMEM;
+        g_ws_bytes[dev] = grow;
+    }
+    *out = g_ws[dev];
+    return QUASAR_OK;
+}
 
 int set_err(quasar_sampler* s, int rc) {
     if (s) s->last_error = rc;
@@ -105,14 +132,17 @@ const char* quasar_status_string(int status) {
     }
 }
 
-int quasar_sampler_pick_batch_launches(void) { return 1; }
+int quasar_sampler_pick_batch_launches(void) { return 2; }
+
+size_t quasar_sampler_workspace_bytes(int B) { return B > 0 ? qs::rows_workspace_bytes(B) : 0; }
 
 int quasar_sampler_pick_batch(const float* d_logits, int64_t ld, int B, int V,
                               const quasar_sample_params* d_params,
                               const quasar_sample_params* h_params, uint64_t* d_rng,
                               int32_t* d_hist, int hist_cap, int32_t* d_hist_len,
                               int32_t* d_hist_head, int record, int32_t* d_out,
-                              quasar_pick_diag* d_diag, int flags, void* stream) {
+                              quasar_pick_diag* d_diag, void* d_workspace, size_t workspace_bytes,
+                              int flags, void* stream) {
     if (B < 0 || V < 1 || V > QUASAR_MAX_VOCAB || ld < V) return QUASAR_EINVAL;
     if (B == 0) return QUASAR_OK;
     if (!d_logits || !d_rng || !d_out || (!d_params && !h_params)) return QUASAR_EINVAL;
@@ -140,7 +170,14 @@ int quasar_sampler_pick_batch(const float* d_logits, int64_t ld, int B, int V,
     a.flags = flags;
     a.vec = ((uintptr_t)d_logits % 32 == 0) && (ld % 8 == 0);
     a.tma = tma && !(flags & QUASAR_FLAG_NO_TMA);
-    const cudaError_t err = qs::launch_sample_rows(a, B, (cudaStream_t)stream);
+    void* ws = d_workspace;
+    if (ws) {
+        if (workspace_bytes < qs::rows_workspace_bytes(B) || (uintptr_t)ws % 256 != 0) return QUASAR_EINVAL;
+    } else {
+        const int rc = managed_workspace(qs::rows_workspace_bytes(B), &ws);
+        if (rc != QUASAR_OK) return rc;
+    }
+    const cudaError_t err = qs::launch_sample_rows(a, ws, (cudaStream_t)stream);
     return err == cudaSuccess ? QUASAR_OK : QUASAR_ECUDA;
 }
 
@@ -244,7 +281,7 @@ int quasar_sampler_pick(quasar_sampler* s, const float* logits, int n_vocab) {
     p.reserved = 0;
     rc = quasar_sampler_pick_batch(d_in, n_vocab, 1, n_vocab, nullptr, &p, s->d_rng, s->d_hist,
                                    s->hist_cap, s->d_meta, s->d_meta + 1, 1, s->d_meta + 2,
-                                   nullptr, 0, s->stream);
+                                   nullptr, nullptr, 0, 0, s->stream);
     if (rc != QUASAR_OK) return set_err(s, rc), -1;
     if (cudaMemcpyAsync(s->h_id, s->d_meta + 2, sizeof(int32_t), cudaMemcpyDeviceToHost,
                         s->stream) != cudaSuccess ||

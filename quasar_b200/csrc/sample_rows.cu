@@ -6,24 +6,25 @@
 //   1. history ring -> shared-memory bitset of penalized ids (sample.c:120)
 //   2. ONE pass over the row from HBM: penalty (sample.c:124), temperature scale
 //      (sample.c:137,142), running max, online window sum of exp(sc - running
-//      max) in double (sample.c:147), and a 16-bit upper bound of each
+//      max) in double (sample.c:147), and a one-byte upper bound of each
 //      thread-tile's max (16 elements) kept in shared memory. Elements more than
 //      30 below the running max contribute < e^-30 each to that sum instead of
 //      being dropped (relative effect < V*e^-30 in the worst case, ~1e-11 on
 //      realistic rows).
 //   3. candidate path (min_p > 0 or top_k <= 256): with the row max known, the
-//      kept prefix lies above a threshold (min-p floor, or the k-th largest tile
-//      max); only thread-tiles whose max clears it are read again (a few % of
+//      kept prefix lies above a threshold (min-p floor, or the k-th largest
+//      per-thread max); only thread-tiles whose bound clears it are read again (a few % of
 //      the row). Their survivors get exact p = (float)exp(sc - max) *
 //      (float)(1/sum), a bitonic sort by (p desc, id asc) (= glibc's stable
 //      qsort of sample.c:151), then the top-k / top-p / min-p cuts and the
 //      inverse-CDF draw with the row's xorshift64* state (sample.c:153-177).
-//   4. select path (any parameters, or when the candidates exceed 2048): an
-//      exact radix select over the p keys of the whole row, re-reading it.
+//   4. select path (any parameters, or when the candidates exceed 4096): the
+//      row is listed in a workspace and a second kernel runs an exact radix
+//      select over the p keys of the whole row, re-reading it.
 // Greedy rows (temperature <= 0) take one pass: penalized argmax, first index
 // on ties, no PRNG step (sample.c:130-134).
 //
-// Two kernels share the per-row code:
+// Two main kernels share the per-row code:
 //   sample_rows_tma  persistent CTAs of 8 consumer warps + 1 producer warp. The
 //                    producer streams the rows' 16 KB chunks with cp.async.bulk
 //                    (TMA, no multicast) into a 3-stage shared-memory ring
@@ -64,10 +65,9 @@ struct Hist {
     unsigned long long mass2[NB];
     int32_t minid2[NB];
 };
-// candidate keys [CAP] followed by the tile-max table; the select path's
-// histograms alias both
-constexpr int SCRATCH_BYTES =
-    (int)sizeof(Hist) > CAP * 8 + TMAX_BYTES ? (int)sizeof(Hist) : CAP * 8 + TMAX_BYTES;
+// candidate keys [CAP] followed by the tile-max table (main kernels); the
+// select kernel keeps its histograms in a layout of its own
+constexpr int SCRATCH_BYTES = CAP * 8 + TMAX_BYTES;
 
 struct Shared {
     int abort;            // a bounded wait gave up
@@ -663,43 +663,102 @@ struct TmaSource {
 };
 
 // ---------------------------------------------------------------------------
-// One row, all consumer threads. Returns nothing; writes out / diag / ring /
-// rng of the row.
-template <class Src>
-__device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src, uint64_t* buf,
-                                            uint32_t* bits, Shared& s) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint8_t* bits8 = reinterpret_cast<const uint8_t*>(bits);
-    Hist* H = reinterpret_cast<Hist*>(buf);
-    const RowParams P = clamp_params(a.d_params ? a.d_params[row] : a.h_params);
-    const int cap = a.hist ? a.hist_cap : 0;
-    int len = 0, head = 0;
-    const int32_t* ring = nullptr;
-    if (cap > 0) {
-        ring = a.hist + (int64_t)row * cap;
-        len = a.hist_len ? min(max(a.hist_len[row], 0), cap) : cap;
-        head = a.hist_head ? ((a.hist_head[row] % cap) + cap) % cap : 0;
+// Per-row set-up and finish shared by the kernels.
+
+struct RowCtx {
+    RowParams P;
+    int cap, len, head;
+    const int32_t* ring;
+};
+
+// Row parameters, history ring and the penalty bitset of `row`.
+__device__ __forceinline__ RowCtx row_setup(const RowsArgs& a, int row, Row& R, uint32_t* bits) {
+    const int tid = threadIdx.x;
+    RowCtx c;
+    c.P = clamp_params(a.d_params ? a.d_params[row] : a.h_params);
+    c.cap = a.hist ? a.hist_cap : 0;
+    c.len = 0;
+    c.head = 0;
+    c.ring = nullptr;
+    if (c.cap > 0) {
+        c.ring = a.hist + (int64_t)row * c.cap;
+        c.len = a.hist_len ? min(max(a.hist_len[row], 0), c.cap) : c.cap;
+        c.head = a.hist_head ? ((a.hist_head[row] % c.cap) + c.cap) % c.cap : 0;
     }
-    Row R;
     R.ptr = a.logits + (int64_t)row * a.ld;
     R.V = a.V;
     R.noct = (a.V + 7) >> 3;
     R.ntiles = (R.noct + OCT_TILE - 1) / OCT_TILE;
     R.vec = a.vec != 0;
-    R.use_pen = P.rp > 1.0f && len > 0;
-    R.rp = P.rp;
-    R.inv_t = 0.0f;
+    R.use_pen = c.P.rp > 1.0f && c.len > 0;
+    R.rp = c.P.rp;
+    R.inv_t = c.P.T > 0.0f ? __fdiv_rn(1.0f, c.P.T) : 0.0f;  // sample.c:137
     R.M = R.thr = R.inv = 0.0f;
     if (R.use_pen) {
-        for (int i = tid; i < len; i += CONSUMERS) {
-            const int id = ring[(head + i) % cap];
+        for (int i = tid; i < c.len; i += CONSUMERS) {
+            const int id = c.ring[(c.head + i) % c.cap];
             if (id >= 0 && id < a.V) atomicOr(&bits[id >> 5], 1u << (id & 31));
         }
     }
     csync();
+    return c;
+}
+
+__device__ __forceinline__ void clear_bits(const RowsArgs& a, const RowCtx& c, const Row& R, uint32_t* bits) {
+    if (R.use_pen) {
+        for (int i = threadIdx.x; i < c.len; i += CONSUMERS) {
+            const int id = c.ring[(c.head + i) % c.cap];
+            if (id >= 0 && id < a.V) bits[id >> 5] = 0u;
+        }
+    }
+}
+
+// Clears the bitset and writes the row's id, report, PRNG state and ring.
+__device__ __forceinline__ void row_finish(const RowsArgs& a, int row, const RowCtx& c, const Row& R,
+                                           uint32_t* bits, int path, uint64_t st_rng, Shared& s) {
+    const int chosen = *reinterpret_cast<volatile int*>(&s.abort) ? -1 : s.res_id;
+    clear_bits(a, c, R, bits);
+    csync();
+    if (threadIdx.x == 0) {
+        if (c.P.T > 0.0f) a.rng[row] = st_rng;
+        a.out[row] = chosen;
+        if (a.diag) {
+            quasar_pick_diag d;
+            d.n_kept = s.res_nc;
+            d.p_chosen = s.res_p;
+            d.inv_sum = R.inv;
+            d.path = path;
+            a.diag[row] = d;
+        }
+        if (a.record && c.cap > 0 && a.hist_len && a.hist_head && chosen >= 0) {
+            int32_t* wring = a.hist + (int64_t)row * c.cap;
+            if (c.len < c.cap) {  // sample.c:85-87
+                wring[(c.head + c.len) % c.cap] = chosen;
+                a.hist_len[row] = c.len + 1;
+            } else {              // sample.c:88-90
+                wring[c.head] = chosen;
+                a.hist_head[row] = (c.head + 1) % c.cap;
+            }
+        }
+    }
+    csync();
+}
+
+// ---------------------------------------------------------------------------
+// One row, all consumer threads. Greedy and candidate-path rows are finished
+// here; a row the candidate path cannot bound is handed to the select kernel
+// (its id, report, PRNG step and ring append are written there).
+template <class Src>
+__device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src, uint64_t* buf,
+                                            uint32_t* bits, Shared& s) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint8_t* bits8 = reinterpret_cast<const uint8_t*>(bits);
+    Row R;
+    const RowCtx c = row_setup(a, row, R, bits);
+    const RowParams& P = c.P;
     src.begin(R);
 
-    int path;
+    int path = QUASAR_PATH_GREEDY;
     uint64_t st_rng = 0;
     if (P.T <= 0.0f) {
         // ---- greedy: penalized argmax, first index on ties ----
@@ -754,194 +813,173 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
             s.res_nc = 0;
             s.res_p = 1.0f;
         }
-        path = QUASAR_PATH_GREEDY;
         csync();
-    } else {
-        // ---- one streaming pass: max, online window sum, tile maxima ----
-        R.inv_t = __fdiv_rn(1.0f, P.T);
-        // slots of the tile-max table: one per thread and group of g tiles
-        const int g = (R.ntiles + TMAX_TILES - 1) / TMAX_TILES;
-        uint8_t* tmax = reinterpret_cast<uint8_t*>(buf) + CAP * 8;
-        float slotmax = -INFINITY;
-        float m = -INFINITY;
-        double S = 0.0;
-        for (int it = 0; it < R.ntiles; it++) {
-            float v[16];
-            src.get(R, it, v, s);
-            const int o0 = it * OCT_TILE + tid, o1 = o0 + CONSUMERS;
-            if (R.use_pen) {
-                const uint32_t m0 = o0 < R.noct ? bits8[o0] : 0u;
-                const uint32_t m1 = o1 < R.noct ? bits8[o1] : 0u;
-                if (m0 | m1) {
-                    apply_pen_oct(v, m0, R.rp);
-                    apply_pen_oct(v + 8, m1, R.rp);
-                }
-            }
-            src.release();
-            // sample.c:142: sc = l * inv_t, rounded exactly like the reference
-            float sc[16];
-#pragma unroll
-            for (int j = 0; j < 16; j++) sc[j] = __fmul_rn(v[j], R.inv_t);
-            float mt = fmaxf(fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3])),
-                             fmaxf(fmaxf(sc[4], sc[5]), fmaxf(sc[6], sc[7])));
-            mt = fmaxf(mt, fmaxf(fmaxf(fmaxf(sc[8], sc[9]), fmaxf(sc[10], sc[11])),
-                                 fmaxf(fmaxf(sc[12], sc[13]), fmaxf(sc[14], sc[15]))));
-            if (mt > m) {
-                S *= exp((double)m - (double)mt);
-                m = mt;
-            }
-            if (m > -INFINITY) {
-                // sample.c:148 against the running max
-                float e[16];
-#pragma unroll
-                for (int j = 0; j < 16; j++) e[j] = sum_term_exp(__fsub_rn(sc[j], m));
-#pragma unroll
-                for (int w = 8; w > 0; w >>= 1)
-#pragma unroll
-                    for (int j = 0; j < w; j++) e[j] += e[j + w];
-                S += (double)e[0];
-            }
-            // upper bound of this thread's max over the slot's tiles (16-bit key)
-            slotmax = fmaxf(slotmax, mt);
-            if (it % g == g - 1 || it == R.ntiles - 1) {
-                tmax[(it / g) * CONSUMERS + tid] = tile_deficit(m, slotmax);
-                slotmax = -INFINITY;
+        row_finish(a, row, c, R, bits, path, st_rng, s);
+        return;
+    }
+
+    // ---- one streaming pass: max, online window sum, tile maxima ----
+    // slots of the tile-max table: one per thread and group of g tiles
+    const int g = (R.ntiles + TMAX_TILES - 1) / TMAX_TILES;
+    uint8_t* tmax = reinterpret_cast<uint8_t*>(buf) + CAP * 8;
+    float slotmax = -INFINITY;
+    float m = -INFINITY;
+    double S = 0.0;
+    for (int it = 0; it < R.ntiles; it++) {
+        float v[16];
+        src.get(R, it, v, s);
+        const int o0 = it * OCT_TILE + tid, o1 = o0 + CONSUMERS;
+        if (R.use_pen) {
+            const uint32_t m0 = o0 < R.noct ? bits8[o0] : 0u;
+            const uint32_t m1 = o1 < R.noct ? bits8[o1] : 0u;
+            if (m0 | m1) {
+                apply_pen_oct(v, m0, R.rp);
+                apply_pen_oct(v + 8, m1, R.rp);
             }
         }
-        s.tfmax[tid] = m;
-        R.M = block_max_f(m, s);
-        const double contrib = (m > -INFINITY) ? S * exp((double)m - (double)R.M) : 0.0;
-        const double Stot = block_sum_d(contrib, s);
-        R.inv = __double2float_rn(1.0 / Stot);
-        R.thr = __fsub_rn(R.M, 30.0f);
+        src.release();
+        // sample.c:142: sc = l * inv_t, rounded exactly like the reference
+        float sc[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) sc[j] = __fmul_rn(v[j], R.inv_t);
+        float mt = fmaxf(fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3])),
+                         fmaxf(fmaxf(sc[4], sc[5]), fmaxf(sc[6], sc[7])));
+        mt = fmaxf(mt, fmaxf(fmaxf(fmaxf(sc[8], sc[9]), fmaxf(sc[10], sc[11])),
+                             fmaxf(fmaxf(sc[12], sc[13]), fmaxf(sc[14], sc[15]))));
+        if (mt > m) {
+            S *= exp((double)m - (double)mt);
+            m = mt;
+        }
+        if (m > -INFINITY) {
+            // sample.c:148 against the running max
+            float e[16];
+#pragma unroll
+            for (int j = 0; j < 16; j++) e[j] = sum_term_exp(__fsub_rn(sc[j], m));
+#pragma unroll
+            for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+                for (int j = 0; j < w; j++) e[j] += e[j + w];
+            S += (double)e[0];
+        }
+        slotmax = fmaxf(slotmax, mt);
+        if (it % g == g - 1 || it == R.ntiles - 1) {
+            tmax[(it / g) * CONSUMERS + tid] = tile_deficit(m, slotmax);
+            slotmax = -INFINITY;
+        }
+    }
+    s.tfmax[tid] = m;
+    R.M = block_max_f(m, s);
+    const double contrib = (m > -INFINITY) ? S * exp((double)m - (double)R.M) : 0.0;
+    const double Stot = block_sum_d(contrib, s);
+    R.inv = __double2float_rn(1.0 / Stot);
+    R.thr = __fsub_rn(R.M, 30.0f);
 
-        // PRNG draw (sample.c:173): one step per stochastic row
-        st_rng = a.rng[row];
-        const double u = rng_unit(&st_rng);
-
-        bool done = false;
-        // Candidate path. The kept prefix lies above a threshold that is known
-        // once M and the tile maxima are: min_p -> sc >= M + ln(min_p) - 0.01
-        // (every p >= min_p * p_max clears it); top_k -> the k-th largest tile
-        // max, less a margin for p ties (k distinct elements reach it). Only the
-        // thread-tiles whose max clears the threshold are read again.
-        const bool by_minp = P.min_p > 0.0f;
-        const bool by_topk = P.top_k > 0 && P.top_k <= TOPK_MAX;
-        if (!(a.flags & QUASAR_FLAG_EXACT_SELECT) && (by_minp || by_topk)) {
-            const int nslot = ((R.ntiles + g - 1) / g) * CONSUMERS;
-            float tau = -INFINITY;
-            if (by_minp) tau = __fadd_rn(R.M, (float)(log((double)fminf(P.min_p, 1.0f)) - 0.01));
-            if (by_topk) tau = fmaxf(tau, topk_floor(P.top_k, s));
-            const float lo = fmaxf(tau, R.thr);
-            if (tid == 0) {
-                s.ncand = 0;
-                s.nq = 0;
+    // Candidate path. The kept prefix lies above a threshold known once M is:
+    // min_p -> sc >= M + ln(min_p) - 0.01 (every p >= min_p * p_max clears
+    // it); top_k -> the k-th largest per-thread max less a tie margin (k
+    // distinct elements reach it). Only thread-tiles whose bound clears the
+    // threshold are read again.
+    const bool by_minp = P.min_p > 0.0f;
+    const bool by_topk = P.top_k > 0 && P.top_k <= TOPK_MAX;
+    bool done = false;
+    if (!(a.flags & QUASAR_FLAG_EXACT_SELECT) && (by_minp || by_topk)) {
+        const int nslot = ((R.ntiles + g - 1) / g) * CONSUMERS;
+        float tau = -INFINITY;
+        if (by_minp) tau = __fadd_rn(R.M, (float)(log((double)fminf(P.min_p, 1.0f)) - 0.01));
+        if (by_topk) tau = fmaxf(tau, topk_floor(P.top_k, s));
+        const float lo = fmaxf(tau, R.thr);
+        if (tid == 0) {
+            s.ncand = 0;
+            s.nq = 0;
+        }
+        csync();
+        // qualifying thread-tiles -> shared list, so the re-reads spread over
+        // all threads and issue in one round
+        uint32_t* qlist = reinterpret_cast<uint32_t*>(buf + CAP / 2);
+        for (int sl = 0; sl * CONSUMERS < nslot; sl++) {
+            if (tile_bound(m, tmax[sl * CONSUMERS + tid]) >= lo) {
+                const int q = atomicAdd(&s.nq, 1);
+                if (q < QMAX) qlist[q] = (uint32_t)(sl * CONSUMERS + tid);
             }
-            csync();
-            // The qualifying thread-tiles go to a shared list first, so the
-            // re-reads spread over all threads and issue in one round.
-            uint32_t* qlist = reinterpret_cast<uint32_t*>(buf + CAP / 2);
-            for (int sl = 0; sl * CONSUMERS < nslot; sl++) {
-                if (tile_bound(m, tmax[sl * CONSUMERS + tid]) >= lo) {
-                    const int q = atomicAdd(&s.nq, 1);
-                    if (q < QMAX) qlist[q] = (uint32_t)(sl * CONSUMERS + tid);
-                }
-            }
-            csync();
-            const int nq_all = s.nq;
-            uint32_t mine[QMAX / CONSUMERS];
+        }
+        csync();
+        const int nq_all = s.nq;
+        uint32_t mine[QMAX / CONSUMERS];
+#pragma unroll
+        for (int k = 0; k < QMAX / CONSUMERS; k++) {
+            const int i = k * CONSUMERS + tid;
+            mine[k] = i < min(nq_all, QMAX) ? qlist[i] : 0xFFFFFFFFu;
+        }
+        csync();  // the list is in registers before candidates overwrite it
+        if (nq_all <= QMAX) {
 #pragma unroll
             for (int k = 0; k < QMAX / CONSUMERS; k++) {
-                const int i = k * CONSUMERS + tid;
-                mine[k] = i < min(nq_all, QMAX) ? qlist[i] : 0xFFFFFFFFu;
-            }
-            csync();  // the list is in registers before candidates overwrite it
-            if (nq_all <= QMAX) {
+                if (mine[k] == 0xFFFFFFFFu) continue;
+                const int sl = (int)(mine[k] / CONSUMERS), owner = (int)(mine[k] % CONSUMERS);
+                for (int it = sl * g; it < min((sl + 1) * g, R.ntiles); it++) {
+                    float v[16];
+                    const int o0 = it * OCT_TILE + owner, o1 = o0 + CONSUMERS;
+                    load_oct(R.ptr, o0, R.V, R.vec, v);
+                    load_oct(R.ptr, o1, R.V, R.vec, v + 8);
+                    if (R.use_pen) {
+                        apply_pen_oct(v, o0 < R.noct ? bits8[o0] : 0u, R.rp);
+                        apply_pen_oct(v + 8, o1 < R.noct ? bits8[o1] : 0u, R.rp);
+                    }
 #pragma unroll
-                for (int k = 0; k < QMAX / CONSUMERS; k++) {
-                    if (mine[k] == 0xFFFFFFFFu) continue;
-                    const int sl = (int)(mine[k] / CONSUMERS), owner = (int)(mine[k] % CONSUMERS);
-                    for (int it = sl * g; it < min((sl + 1) * g, R.ntiles); it++) {
-                        float v[16];
-                        const int o0 = it * OCT_TILE + owner, o1 = o0 + CONSUMERS;
-                        load_oct(R.ptr, o0, R.V, R.vec, v);
-                        load_oct(R.ptr, o1, R.V, R.vec, v + 8);
-                        if (R.use_pen) {
-                            apply_pen_oct(v, o0 < R.noct ? bits8[o0] : 0u, R.rp);
-                            apply_pen_oct(v + 8, o1 < R.noct ? bits8[o1] : 0u, R.rp);
-                        }
-#pragma unroll
-                        for (int j = 0; j < 16; j++) {
-                            const float sc = __fmul_rn(v[j], R.inv_t);
-                            const int idx = j < 8 ? 8 * o0 + j : 8 * o1 + (j - 8);
-                            if (sc >= lo && idx < R.V) {
-                                const int pos = atomicAdd(&s.ncand, 1);
-                                if (pos < CAP)
-                                    buf[pos] = ((uint64_t)p_key(sc, R.M, R.thr, R.inv) << 32) |
-                                               (uint32_t)(~(uint32_t)idx);
-                            }
+                    for (int j = 0; j < 16; j++) {
+                        const float sc = __fmul_rn(v[j], R.inv_t);
+                        const int idx = j < 8 ? 8 * o0 + j : 8 * o1 + (j - 8);
+                        if (sc >= lo && idx < R.V) {  // raw (sc, id); p is computed below
+                            const int pos = atomicAdd(&s.ncand, 1);
+                            if (pos < CAP) buf[pos] = ((uint64_t)__float_as_uint(sc) << 32) | (uint32_t)idx;
                         }
                     }
                 }
             }
-            csync();
-            const int nk = nq_all <= QMAX ? s.ncand : CAP + 1;
-            if (nk > 0 && nk <= CAP) {
-                int n2 = 1;
-                while (n2 < nk) n2 <<= 1;
-                for (int i = nk + tid; i < n2; i += CONSUMERS) buf[i] = 0ull;
-                csync();
-                bitonic_desc(buf, n2);
-                if (tid < 32) candidate_cuts(buf, nk, P, by_minp ? __fmul_rn(P.min_p, R.inv) : 0.0f, u, s);
-                done = true;
-                path = QUASAR_PATH_CANDIDATE;
+        }
+        csync();
+        const int nk = nq_all <= QMAX ? s.ncand : CAP + 1;
+        if (nk > 0 && nk <= CAP) {
+            int n2 = 1;
+            while (n2 < nk) n2 <<= 1;
+            for (int i = tid; i < n2; i += CONSUMERS) {
+                uint64_t key = 0ull;
+                if (i < nk) {
+                    const uint64_t e = buf[i];
+                    const float sc = __uint_as_float((uint32_t)(e >> 32));
+                    key = ((uint64_t)p_key(sc, R.M, R.thr, R.inv) << 32) | (uint32_t)(~(uint32_t)e);
+                }
+                buf[i] = key;
             }
             csync();
+            bitonic_desc(buf, n2);
+            st_rng = a.rng[row];
+            const double u = rng_unit(&st_rng);  // sample.c:173: one step per stochastic row
+            if (tid < 32) candidate_cuts(buf, nk, P, by_minp ? __fmul_rn(P.min_p, R.inv) : 0.0f, u, s);
+            done = true;
+            path = QUASAR_PATH_CANDIDATE;
         }
-        if (!done) {
-            csync();
-            select_path(R, bits8, H, P, u, s);
-            path = QUASAR_PATH_SELECT;
-        }
+        csync();
     }
-
-    // ---- epilogue: clear the bitset, record, outputs ----
-    const int chosen = *reinterpret_cast<volatile int*>(&s.abort) ? -1 : s.res_id;
-    if (R.use_pen) {
-        for (int i = tid; i < len; i += CONSUMERS) {
-            const int id = ring[(head + i) % cap];
-            if (id >= 0 && id < a.V) bits[id >> 5] = 0u;
+    if (!done) {
+        // the exact select path runs in sample_rows_select over the listed rows
+        if (tid == 0) {
+            const int i = atomicAdd(a.work_count, 1);
+            a.work_rows[i] = row;
+            a.work_M[i] = R.M;
+            a.work_inv[i] = R.inv;
         }
+        clear_bits(a, c, R, bits);
+        csync();
+        return;
     }
-    csync();
-    if (tid == 0) {
-        if (P.T > 0.0f) a.rng[row] = st_rng;
-        a.out[row] = chosen;
-        if (a.diag) {
-            quasar_pick_diag d;
-            d.n_kept = s.res_nc;
-            d.p_chosen = s.res_p;
-            d.inv_sum = R.inv;
-            d.path = path;
-            a.diag[row] = d;
-        }
-        if (a.record && cap > 0 && a.hist_len && a.hist_head && chosen >= 0) {
-            int32_t* wring = a.hist + (int64_t)row * cap;
-            if (len < cap) {
-                wring[(head + len) % cap] = chosen;
-                a.hist_len[row] = len + 1;
-            } else {
-                wring[head] = chosen;
-                a.hist_head[row] = (head + 1) % cap;
-            }
-        }
-    }
-    csync();
+    row_finish(a, row, c, R, bits, path, st_rng, s);
 }
 
 // ---------------------------------------------------------------------------
 // Dynamic shared memory of the LDG kernel: [scratch][bits]; of the TMA kernel:
-// [ring NSTAGE x 16 KB][scratch][bits][full bars][empty bars].
+// [ring NSTAGE x 16 KB][scratch][bits][full bars][empty bars]; of the select
+// kernel: [Hist][bits].
 
 __global__ void __launch_bounds__(CONSUMERS, 3) sample_rows_ldg(RowsArgs a) {
     extern __shared__ __align__(128) unsigned char dyn[];
@@ -966,8 +1004,8 @@ __global__ void __launch_bounds__(CONSUMERS + 32, 2) sample_rows_tma(RowsArgs a)
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + NSTAGE);
     if (threadIdx.x == 0) {
         for (int i = 0; i < NSTAGE; i++) {
-            mbar_init(full0 + 8u * i, 1);            // producer's arrive.expect_tx
-            mbar_init(empty0 + 8u * i, CWARPS);     // one arrival per consumer warp
+            mbar_init(full0 + 8u * i, 1);          // producer's arrive.expect_tx
+            mbar_init(empty0 + 8u * i, CWARPS);   // one arrival per consumer warp
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         s.abort = 0;
@@ -1016,6 +1054,34 @@ __global__ void __launch_bounds__(CONSUMERS + 32, 2) sample_rows_tma(RowsArgs a)
     }
 }
 
+// Rows the candidate path handed over: exact radix select over the whole row
+// (re-reading it), then the row's outputs. Runs after the main kernel on the
+// same stream, so the list is complete; with no listed row it exits at once.
+__global__ void __launch_bounds__(CONSUMERS) sample_rows_select(RowsArgs a) {
+    extern __shared__ __align__(128) unsigned char dyn[];
+    Hist* H = reinterpret_cast<Hist*>(dyn);
+    uint32_t* bits = reinterpret_cast<uint32_t*>(dyn + sizeof(Hist));
+    const uint8_t* bits8 = reinterpret_cast<const uint8_t*>(bits);
+    __shared__ Shared s;
+    const int n = *a.work_count;
+    if ((int)blockIdx.x >= n) return;
+    for (int i = threadIdx.x; i < a.nwords; i += CONSUMERS) bits[i] = 0u;
+    if (threadIdx.x == 0) s.abort = 0;
+    csync();
+    for (int i = blockIdx.x; i < n; i += gridDim.x) {
+        const int row = a.work_rows[i];
+        Row R;
+        const RowCtx c = row_setup(a, row, R, bits);
+        R.M = a.work_M[i];
+        R.inv = a.work_inv[i];
+        R.thr = __fsub_rn(R.M, 30.0f);
+        uint64_t st = a.rng[row];
+        const double u = rng_unit(&st);  // sample.c:173
+        select_path(R, bits8, H, c.P, u, s);
+        row_finish(a, row, c, R, bits, QUASAR_PATH_SELECT, st, s);
+    }
+}
+
 }  // namespace rows
 
 static int nwords_for(int V) { return ((V + 31) >> 5) + 1; }
@@ -1029,53 +1095,75 @@ size_t rows_tma_smem_bytes(int V) {
            (((size_t)nwords_for(V) * 4 + 7) & ~(size_t)7) + 2 * rows::NSTAGE * sizeof(uint64_t);
 }
 
+size_t rows_select_smem_bytes(int V) {
+    return sizeof(rows::Hist) + (size_t)nwords_for(V) * sizeof(uint32_t);
+}
+
+size_t rows_workspace_bytes(int B) {
+    return (size_t)256 + (size_t)B * 12 + 256;
+}
+
 int rows_threads() { return rows::CONSUMERS; }
 
 namespace {
 struct KernelCfg {
     size_t smem_set[64];
-    int persistent[64];  // resident CTAs per device for the TMA kernel
+    int grid[64];  // persistent grid of the kernel on each device
 };
-thread_local KernelCfg g_ldg = {}, g_tma = {};
+thread_local KernelCfg g_ldg = {}, g_tma = {}, g_sel = {};
+
+cudaError_t configure(KernelCfg& cfg, const void* fn, int threads, size_t smem, int dev) {
+    cudaError_t err = cudaSuccess;
+    if (cfg.smem_set[dev] < smem) {
+        err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (err != cudaSuccess) return err;
+        cfg.smem_set[dev] = smem;
+        cfg.grid[dev] = 0;
+    }
+    if (cfg.grid[dev] == 0) {
+        int per_sm = 0, sms = 0;
+        err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem);
+        if (err != cudaSuccess) return err;
+        err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (err != cudaSuccess) return err;
+        cfg.grid[dev] = max(1, per_sm) * sms;
+    }
+    return cudaSuccess;
+}
 }  // namespace
 
-cudaError_t launch_sample_rows(const RowsArgs& args, int grid, cudaStream_t stream) {
+cudaError_t launch_sample_rows(const RowsArgs& args, void* workspace, cudaStream_t stream) {
     RowsArgs a = args;
     a.nwords = nwords_for(args.V);
+    // workspace: [count][pad][rows B][M B][inv B]
+    char* ws = reinterpret_cast<char*>(workspace);
+    a.work_count = reinterpret_cast<int*>(ws);
+    a.work_rows = reinterpret_cast<int*>(ws + 256);
+    a.work_M = reinterpret_cast<float*>(ws + 256 + (size_t)args.B * 4);
+    a.work_inv = reinterpret_cast<float*>(ws + 256 + (size_t)args.B * 8);
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
     if (err != cudaSuccess) return err;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    err = cudaMemsetAsync(a.work_count, 0, sizeof(int), stream);
+    if (err != cudaSuccess) return err;
     if (a.tma) {
         const size_t smem = rows_tma_smem_bytes(a.V);
-        if (g_tma.smem_set[dev] < smem) {
-            err = cudaFuncSetAttribute(rows::sample_rows_tma, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
-            if (err != cudaSuccess) return err;
-            g_tma.smem_set[dev] = smem;
-            g_tma.persistent[dev] = 0;
-        }
-        if (g_tma.persistent[dev] == 0) {
-            int per_sm = 0, sms = 0;
-            err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rows::sample_rows_tma,
-                                                                rows::CONSUMERS + 32, smem);
-            if (err != cudaSuccess) return err;
-            err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-            if (err != cudaSuccess) return err;
-            g_tma.persistent[dev] = max(1, per_sm) * sms;
-        }
-        const int g = min(grid, g_tma.persistent[dev]);
-        rows::sample_rows_tma<<<g, rows::CONSUMERS + 32, smem, stream>>>(a);
+        err = configure(g_tma, (const void*)rows::sample_rows_tma, rows::CONSUMERS + 32, smem, dev);
+        if (err != cudaSuccess) return err;
+        rows::sample_rows_tma<<<min(a.B, g_tma.grid[dev]), rows::CONSUMERS + 32, smem, stream>>>(a);
     } else {
         const size_t smem = rows_smem_bytes(a.V);
-        if (g_ldg.smem_set[dev] < smem) {
-            err = cudaFuncSetAttribute(rows::sample_rows_ldg, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
-            if (err != cudaSuccess) return err;
-            g_ldg.smem_set[dev] = smem;
-        }
-        rows::sample_rows_ldg<<<grid, rows::CONSUMERS, smem, stream>>>(a);
+        err = configure(g_ldg, (const void*)rows::sample_rows_ldg, rows::CONSUMERS, smem, dev);
+        if (err != cudaSuccess) return err;
+        rows::sample_rows_ldg<<<a.B, rows::CONSUMERS, smem, stream>>>(a);
     }
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    const size_t ssmem = rows_select_smem_bytes(a.V);
+    err = configure(g_sel, (const void*)rows::sample_rows_select, rows::CONSUMERS, ssmem, dev);
+    if (err != cudaSuccess) return err;
+    rows::sample_rows_select<<<min(a.B, g_sel.grid[dev]), rows::CONSUMERS, ssmem, stream>>>(a);
     return cudaGetLastError();
 }
 

@@ -100,7 +100,7 @@ def params_to_device(params: np.ndarray, device):
 
 def pick_batch(logits, rng, *, params=None, d_params=None, hist=None, hist_len=None,
                hist_head=None, record: bool = False, out=None, diag=None,
-               flags: int = 0, stream=None):
+               workspace=None, flags: int = 0, stream=None):
     """Sample every row of ``logits`` ([B, V] float32 CUDA tensor, unit column stride).
 
     rng: [B] int64 CUDA tensor holding xorshift64* states (advanced in place).
@@ -108,8 +108,10 @@ def pick_batch(logits, rng, *, params=None, d_params=None, hist=None, hist_len=N
     uint8 CUDA tensor from ``params_to_device`` with one record per row.
     hist / hist_len / hist_head: int32 CUDA tensors [B, H] / [B] / [B].
     out: optional int32 [B] CUDA tensor; diag: optional int32 [B, 4] CUDA tensor
-    (DIAG_DTYPE records). Returns ``out``. Launches on ``stream`` (a
-    torch.cuda.Stream; default: the current stream).
+    (DIAG_DTYPE records). workspace: optional uint8 CUDA tensor of at least
+    ``workspace_bytes(B)`` bytes (default: the library's per-device one).
+    Returns ``out``. Launches on ``stream`` (a torch.cuda.Stream; default: the
+    current stream).
     """
     import torch
     if logits.dim() != 2 or logits.dtype != torch.float32 or logits.stride(1) != 1:
@@ -133,9 +135,15 @@ def pick_batch(logits, rng, *, params=None, d_params=None, hist=None, hist_len=N
         _ptr(logits), logits.stride(0), B, V, _ptr(d_params),
         None if hp is None else ctypes.byref(hp), _ptr(rng), _ptr(hist), H,
         _ptr(hist_len), _ptr(hist_head), 1 if record else 0, _ptr(out), _ptr(diag),
+        _ptr(workspace), 0 if workspace is None else workspace.numel() * workspace.element_size(),
         int(flags), ctypes.c_void_p(stream.cuda_stream))
     check(rc, "quasar_sampler_pick_batch")
     return out
+
+
+def workspace_bytes(B: int) -> int:
+    """Bytes of device workspace one pick_batch call over B rows needs."""
+    return int(lib().quasar_sampler_workspace_bytes(int(B)))
 
 
 def synth_logits(kind: int, seed: int, row0: int, B: int, V: int, scale: float, out, stream=None):
@@ -163,6 +171,6 @@ def synth_uniform(seed: int, row0: int, B: int, lo: float, hi: float, out, strea
     return out
 
 
-__all__ = ["Sampler", "SampleParams", "make_params", "params_to_device", "pick_batch",
+__all__ = ["Sampler", "SampleParams", "make_params", "params_to_device", "pick_batch", "workspace_bytes",
            "synth_logits", "synth_hist", "synth_uniform", "PARAMS_DTYPE", "DIAG_DTYPE",
            "FLAG_EXACT_SELECT"]

@@ -59,7 +59,7 @@ def test_batch_rejects_bad_shapes(B, V, ld):
     lib = q.lib()
     rc = lib.quasar_sampler_pick_batch(ctypes.c_void_p(16), ld, B, V, None, None,
                                        ctypes.c_void_p(16), None, 0, None, None, 0,
-                                       ctypes.c_void_p(16), None, 0, None)
+                                       ctypes.c_void_p(16), None, None, 0, 0, None)
     assert rc == -1
 
 
@@ -69,17 +69,21 @@ def test_batch_rejects_missing_pointers():
     P = ctypes.c_void_p
     # no params at all
     assert lib.quasar_sampler_pick_batch(P(16), 10, 1, 10, None, None, P(16), None, 0, None, None,
-                                         0, P(16), None, 0, None) == -1
+                                         0, P(16), None, None, 0, 0, None) == -1
     prm = q.SampleParams(1.0, 1.0, 0.0, 1.0, 0, 0)
     # history capacity without a ring
     assert lib.quasar_sampler_pick_batch(P(16), 10, 1, 10, None, ctypes.byref(prm), P(16), None, 4,
-                                         None, None, 0, P(16), None, 0, None) == -1
+                                         None, None, 0, P(16), None, None, 0, 0, None) == -1
     # record without len/head
     assert lib.quasar_sampler_pick_batch(P(16), 10, 1, 10, None, ctypes.byref(prm), P(16), P(16), 4,
-                                         None, None, 1, P(16), None, 0, None) == -1
+                                         None, None, 1, P(16), None, None, 0, 0, None) == -1
     # B == 0 is a no-op
     assert lib.quasar_sampler_pick_batch(None, 10, 0, 10, None, None, None, None, 0, None, None, 0,
-                                         None, None, 0, None) == 0
+                                         None, None, None, 0, 0, None) == 0
+    # an explicit workspace must be large enough and 256-byte aligned
+    assert lib.quasar_sampler_pick_batch(P(16), 10, 1, 10, None, ctypes.byref(prm), P(16), None, 0,
+                                         None, None, 0, P(16), None, P(256), 8, 0, None) == -1
+    assert lib.quasar_sampler_workspace_bytes(4096) >= 4096 * 12
 
 
 def test_pick_guards_without_gpu():
