@@ -84,6 +84,8 @@ struct Shared {
     float pf_lo, pf_hi;
     int res_id, res_nc, res_pos;
     float res_p;
+    int cut_p, cut_m, cut_d;  // candidate cuts (atomicMin targets)
+    double rsum;
 };
 
 // Barrier of the 256 consumer threads (warps 0-7); the TMA producer warp never
@@ -507,66 +509,159 @@ __device__ void select_path(const Row& R, const uint8_t* bits8, Hist* H,
     csync();
 }
 
-// Candidate path over the sorted list keys[0, nk): cuts and draw. Warp 0 only.
+// Candidate path over the sorted list keys[0, nk): cuts and draw by all
+// consumer threads. Thread t owns the contiguous positions [t*L, t*L + L);
+// cumulative sums are per-thread double sums joined by a block scan (the
+// reference's sequential double cumsum, regrouped: equal up to ~1e-16).
 __device__ void candidate_cuts(const uint64_t* keys, int nk, const RowParams& P, float floor_p,
                                double u, Shared& s) {
-    const int lane = threadIdx.x & 31;
-    auto pval = [&](int i) { return __uint_as_float((uint32_t)(keys[i] >> 32)); };
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int BEYOND = 0x7FFFFFFF;
-    // top-k: a cut inside the list is exact; a larger k lies beyond the min-p cut
+    auto pval = [&](int i) { return __uint_as_float((uint32_t)(keys[i] >> 32)); };
+    const int L = (nk + CONSUMERS - 1) / CONSUMERS;
+    const int i0 = min(tid * L, nk), i1 = min(i0 + L, nk);
+    double seg = 0.0;
+    for (int i = i0; i < i1; i++) seg += (double)pval(i);
+    const double incl = warp_incl_scan(seg, lane);
+    if (lane == 31) s.rd[w] = incl;
+    if (tid == 0) {
+        s.cut_p = BEYOND;
+        s.cut_m = nk;
+        s.cut_d = BEYOND;
+    }
+    csync();
+    double excl = incl - seg;
+    for (int k = 0; k < w; k++) excl += s.rd[k];
+    // top-k (sample.c:154): a cut inside the list is exact; a larger k lies
+    // beyond the list's own bound
     const int nc1 = (P.top_k > 0 && P.top_k < nk) ? P.top_k : BEYOND;
     const int lim = min(nc1, nk);
-    int nc2 = nc1;
+    // top-p (sample.c:156-160): first prefix whose cumsum reaches top_p
     if (P.top_p < 1.0f) {
-        double carry = 0.0;
-        for (int base = 0; base < lim; base += 32) {
-            const int i = base + lane;
-            const double p = i < lim ? (double)pval(i) : 0.0;
-            const double c = warp_incl_scan(p, lane) + carry;
-            const unsigned bal = __ballot_sync(FULL, i < lim && c >= (double)P.top_p);
-            if (bal) {
-                nc2 = base + __ffs(bal);
+        double c = excl;
+        for (int i = i0; i < min(i1, lim); i++) {
+            c += (double)pval(i);
+            if (c >= (double)P.top_p) {
+                atomicMin(&s.cut_p, i + 1);
                 break;
             }
-            carry = __shfl_sync(FULL, c, 31);
         }
     }
-    // min-p: first i >= 1 below the floor; every element outside the list is
-    // below the floor, so "not found" means nk
-    int fb = nk;
-    for (int base = 0; base < nk; base += 32) {
-        const int i = base + lane;
-        const unsigned bal = __ballot_sync(FULL, i >= 1 && i < nk && pval(i) < floor_p);
-        if (bal) {
-            fb = base + __ffs(bal) - 1;
+    // min-p (sample.c:162-167): first i >= 1 below the floor; every element
+    // outside the list is below the floor, so "none" means nk
+    for (int i = max(i0, 1); i < i1; i++)
+        if (pval(i) < floor_p) {
+            atomicMin(&s.cut_m, i);
             break;
         }
+    csync();
+    const int nc2 = s.cut_p != BEYOND ? s.cut_p : nc1;
+    const int nc = max(1, min(nc2, s.cut_m));
+    if (nc - 1 >= i0 && nc - 1 < i1) {  // the kept mass (sample.c:171-172)
+        double c = excl;
+        for (int i = i0; i < nc; i++) c += (double)pval(i);
+        s.rsum = c;
     }
-    int nc = min(nc2, fb);
-    if (nc < 1) nc = 1;
-    // draw
-    double part = 0.0;
-    for (int i = lane; i < nc; i += 32) part += (double)pval(i);
-    const double rsum = warp_sum(part);
-    const double r = u * rsum;
-    int chosen = nc - 1;
-    double carry = 0.0;
-    for (int base = 0; base < nc; base += 32) {
-        const int i = base + lane;
-        const double p = i < nc ? (double)pval(i) : 0.0;
-        const double c = warp_incl_scan(p, lane) + carry;
-        const unsigned bal = __ballot_sync(FULL, i < nc && c >= r);
-        if (bal) {
-            chosen = base + __ffs(bal) - 1;
-            break;
+    csync();
+    const double r = u * s.rsum;  // sample.c:173-175
+    {
+        double c = excl;
+        for (int i = i0; i < min(i1, nc); i++) {
+            c += (double)pval(i);
+            if (c >= r) {
+                atomicMin(&s.cut_d, i);
+                break;
+            }
         }
-        carry = __shfl_sync(FULL, c, 31);
     }
-    if (lane == 0) {
+    csync();
+    if (tid == 0) {
+        const int chosen = s.cut_d != BEYOND ? s.cut_d : nc - 1;
         s.res_id = (int)(~(uint32_t)keys[chosen]);
         s.res_nc = nc;
         s.res_p = pval(chosen);
     }
+    csync();
+}
+
+__device__ __forceinline__ void cx_desc(uint64_t& a, uint64_t& b, bool desc) {
+    const uint64_t hi = a > b ? a : b, lo = a > b ? b : a;
+    a = desc ? hi : lo;
+    b = desc ? lo : hi;
+}
+
+// Bitonic sort, descending, of n2 = 256*E keys held E per lane: warp w owns
+// positions w*C + q*32 + lane (C = 32*E, q < E). Exchanges across lanes use
+// shuffles, across a lane's own registers plain compares, and only exchanges
+// across warps go through shared memory (sm) and the consumer barrier.
+template <int E>
+__device__ void sort_regs_desc(uint64_t (&v)[E], uint64_t* sm) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    constexpr int C = 32 * E;
+    constexpr int N2 = CONSUMERS * E;
+    for (int k = 2; k <= N2; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            if (j >= C) {
+#pragma unroll
+                for (int q = 0; q < E; q++) sm[w * C + q * 32 + lane] = v[q];
+                csync();
+#pragma unroll
+                for (int q = 0; q < E; q++) {
+                    const int i = w * C + q * 32 + lane;
+                    const uint64_t x = sm[i ^ j];
+                    const bool first = (i & j) == 0, desc = (i & k) == 0;
+                    const uint64_t hi = v[q] > x ? v[q] : x, lo = v[q] > x ? x : v[q];
+                    v[q] = (first == desc) ? hi : lo;
+                }
+                csync();
+            } else if (j >= 32) {
+                const int jb = j >> 5;
+#pragma unroll
+                for (int q = 0; q < E; q++) {
+#pragma unroll
+                    for (int b = 1; b < E; b <<= 1) {
+                        if (b == jb && (q & b) == 0) {
+                            const int i = w * C + q * 32 + lane;
+                            cx_desc(v[q], v[q | b], (i & k) == 0);
+                        }
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int q = 0; q < E; q++) {
+                    const int i = w * C + q * 32 + lane;
+                    const uint64_t x = __shfl_xor_sync(FULL, v[q], j);
+                    const bool first = (lane & j) == 0, desc = (i & k) == 0;
+                    const uint64_t hi = v[q] > x ? v[q] : x, lo = v[q] > x ? x : v[q];
+                    v[q] = (first == desc) ? hi : lo;
+                }
+            }
+        }
+    }
+}
+
+// Converts the nk raw (sc, id) entries raw[0, nk) into (p, ~id) keys, sorts
+// them descending and leaves them in buf[0, 256*E) (zero keys past nk).
+template <int E>
+__device__ void keys_sorted(uint64_t* buf, const uint64_t* raw, int nk, const Row& R) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    constexpr int C = 32 * E;
+    uint64_t v[E];
+#pragma unroll
+    for (int q = 0; q < E; q++) {
+        const int i = w * C + q * 32 + lane;
+        v[q] = 0ull;
+        if (i < nk) {
+            const uint64_t e = raw[i];
+            const float sc = __uint_as_float((uint32_t)(e >> 32));
+            v[q] = ((uint64_t)p_key(sc, R.M, R.thr, R.inv) << 32) | (uint32_t)(~(uint32_t)e);
+        }
+    }
+    csync();  // every raw entry is in registers before buf is reused
+    sort_regs_desc<E>(v, buf);
+#pragma unroll
+    for (int q = 0; q < E; q++) buf[w * C + q * 32 + lane] = v[q];
+    csync();
 }
 
 // Tile-max table entry: how far (in 1/8 nat, rounded down, saturating at 255)
@@ -893,9 +988,10 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
             s.nq = 0;
         }
         csync();
-        // qualifying thread-tiles -> shared list, so the re-reads spread over
-        // all threads and issue in one round
-        uint32_t* qlist = reinterpret_cast<uint32_t*>(buf + CAP / 2);
+        // qualifying thread-tiles -> a shared list (bottom of buf), so the
+        // re-reads spread over all threads and issue in one round; raw
+        // survivors are appended from the top of buf downwards
+        uint32_t* qlist = reinterpret_cast<uint32_t*>(buf);
         for (int sl = 0; sl * CONSUMERS < nslot; sl++) {
             if (tile_bound(m, tmax[sl * CONSUMERS + tid]) >= lo) {
                 const int q = atomicAdd(&s.nq, 1);
@@ -904,34 +1000,45 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
         }
         csync();
         const int nq_all = s.nq;
-        uint32_t mine[QMAX / CONSUMERS];
-#pragma unroll
-        for (int k = 0; k < QMAX / CONSUMERS; k++) {
-            const int i = k * CONSUMERS + tid;
-            mine[k] = i < min(nq_all, QMAX) ? qlist[i] : 0xFFFFFFFFu;
-        }
-        csync();  // the list is in registers before candidates overwrite it
-        if (nq_all <= QMAX) {
-#pragma unroll
-            for (int k = 0; k < QMAX / CONSUMERS; k++) {
-                if (mine[k] == 0xFFFFFFFFu) continue;
-                const int sl = (int)(mine[k] / CONSUMERS), owner = (int)(mine[k] % CONSUMERS);
-                for (int it = sl * g; it < min((sl + 1) * g, R.ntiles); it++) {
-                    float v[16];
-                    const int o0 = it * OCT_TILE + owner, o1 = o0 + CONSUMERS;
-                    load_oct(R.ptr, o0, R.V, R.vec, v);
-                    load_oct(R.ptr, o1, R.V, R.vec, v + 8);
+        const int nq = min(nq_all, QMAX);
+        const int room = CAP - (nq + 1) / 2;  // entries left above the list
+        for (int base = 0; base < nq; base += CONSUMERS) {
+            const int i = base + tid;
+            const uint32_t entry = i < nq ? qlist[i] : 0u;
+            const int sl = (int)(entry / CONSUMERS), owner = (int)(entry % CONSUMERS);
+            for (int t = 0; t < g; t++) {
+                const int it = sl * g + t;
+                const bool ok = i < nq && it < R.ntiles;
+                const int o0 = it * OCT_TILE + owner, o1 = o0 + CONSUMERS;
+                float sc[16];
+                uint32_t mask = 0u;
+                if (ok) {
+                    load_oct(R.ptr, o0, R.V, R.vec, sc);
+                    load_oct(R.ptr, o1, R.V, R.vec, sc + 8);
                     if (R.use_pen) {
-                        apply_pen_oct(v, o0 < R.noct ? bits8[o0] : 0u, R.rp);
-                        apply_pen_oct(v + 8, o1 < R.noct ? bits8[o1] : 0u, R.rp);
+                        apply_pen_oct(sc, o0 < R.noct ? bits8[o0] : 0u, R.rp);
+                        apply_pen_oct(sc + 8, o1 < R.noct ? bits8[o1] : 0u, R.rp);
                     }
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
-                        const float sc = __fmul_rn(v[j], R.inv_t);
+                        sc[j] = __fmul_rn(sc[j], R.inv_t);
                         const int idx = j < 8 ? 8 * o0 + j : 8 * o1 + (j - 8);
-                        if (sc >= lo && idx < R.V) {  // raw (sc, id); p is computed below
-                            const int pos = atomicAdd(&s.ncand, 1);
-                            if (pos < CAP) buf[pos] = ((uint64_t)__float_as_uint(sc) << 32) | (uint32_t)idx;
+                        mask |= (sc[j] >= lo && idx < R.V ? 1u : 0u) << j;
+                    }
+                }
+                // one shared atomic per warp reserves the slots
+                const int cnt = __popc(mask);
+                const int incl = warp_incl_scan(cnt, lane);
+                int pos = 0;
+                if (lane == 31 && incl > 0) pos = atomicAdd(&s.ncand, incl);
+                pos = __shfl_sync(FULL, pos, 31) + incl - cnt;
+                if (mask) {
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        if (mask & (1u << j)) {
+                            const int idx = j < 8 ? 8 * o0 + j : 8 * o1 + (j - 8);
+                            if (pos < room) buf[CAP - 1 - pos] = ((uint64_t)__float_as_uint(sc[j]) << 32) | (uint32_t)idx;
+                            pos++;
                         }
                     }
                 }
@@ -939,23 +1046,29 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
         }
         csync();
         const int nk = nq_all <= QMAX ? s.ncand : CAP + 1;
-        if (nk > 0 && nk <= CAP) {
-            int n2 = 1;
-            while (n2 < nk) n2 <<= 1;
-            for (int i = tid; i < n2; i += CONSUMERS) {
-                uint64_t key = 0ull;
-                if (i < nk) {
-                    const uint64_t e = buf[i];
-                    const float sc = __uint_as_float((uint32_t)(e >> 32));
-                    key = ((uint64_t)p_key(sc, R.M, R.thr, R.inv) << 32) | (uint32_t)(~(uint32_t)e);
+        if (nk > 0 && nk <= room) {
+            const uint64_t* keys = buf;
+            // raw entries live in buf[CAP - nk, CAP)
+            if (nk <= 256) keys_sorted<1>(buf, buf + CAP - nk, nk, R);
+            else if (nk <= 512) keys_sorted<2>(buf, buf + CAP - nk, nk, R);
+            else if (nk <= 1024) keys_sorted<4>(buf, buf + CAP - nk, nk, R);
+            else {
+                int n2 = 2048;
+                while (n2 < nk) n2 <<= 1;
+                uint64_t* area = buf + CAP - n2;  // n2 <= CAP: in place, padded below
+                for (int i = tid; i < n2 - nk; i += CONSUMERS) area[i] = 0ull;
+                for (int i = n2 - nk + tid; i < n2; i += CONSUMERS) {
+                    const uint64_t e = area[i];
+                    const float v = __uint_as_float((uint32_t)(e >> 32));
+                    area[i] = ((uint64_t)p_key(v, R.M, R.thr, R.inv) << 32) | (uint32_t)(~(uint32_t)e);
                 }
-                buf[i] = key;
+                csync();
+                bitonic_desc(area, n2);
+                keys = area;
             }
-            csync();
-            bitonic_desc(buf, n2);
             st_rng = a.rng[row];
             const double u = rng_unit(&st_rng);  // sample.c:173: one step per stochastic row
-            if (tid < 32) candidate_cuts(buf, nk, P, by_minp ? __fmul_rn(P.min_p, R.inv) : 0.0f, u, s);
+            candidate_cuts(keys, nk, P, by_minp ? __fmul_rn(P.min_p, R.inv) : 0.0f, u, s);
             done = true;
             path = QUASAR_PATH_CANDIDATE;
         }
