@@ -95,6 +95,66 @@ __device__ __forceinline__ float exp_poly(float x) {
     return __int_as_float(__float_as_int(p) + (k << 23));
 }
 
+// ---- packed fp32x2 arithmetic (sm_100: one instruction for two lanes, each
+// lane an IEEE round-to-nearest operation, so results equal the scalar ops) ----
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 pack2(float lo, float hi) {
+    f32x2 r;
+    asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void unpack2(f32x2 v, float& lo, float& hi) {
+    asm("mov.b64 {%0,%1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
+    f32x2 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
+    f32x2 d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ f32x2 mul2(f32x2 a, f32x2 b) {
+    f32x2 d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// max of three (sm_100 three-input max.f32; NaN inputs are ignored like fmaxf)
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// exp_poly on two lanes at once: the same operations in the same order, so
+// each lane's result equals exp_poly of that lane.
+__device__ __forceinline__ f32x2 exp_poly2(float a, float b) {
+    const f32x2 kLog2e = 0x3fb8aa3b3fb8aa3bull, kMagic = 0x4b4000004b400000ull,
+                kNegMagic = 0xcb400000cb400000ull, kNegHi = 0xbf318000bf318000ull,
+                kLo = 0x395e8083395e8083ull, kC6 = 0x3ab543d63ab543d6ull, kC5 = 0x3c0936563c093656ull,
+                kC4 = 0x3d2aac713d2aac71ull, kC3 = 0x3e2aaa063e2aaa06ull, kC2 = 0x3efffffd3efffffdull,
+                kOne = 0x3f8000003f800000ull;
+    const f32x2 x = pack2(fmaxf(a, -86.0f), fmaxf(b, -86.0f));
+    const f32x2 t = fma2(x, kLog2e, kMagic);
+    const f32x2 kf = add2(t, kNegMagic);
+    f32x2 r = fma2(kf, kNegHi, x);
+    r = fma2(kf, kLo, r);
+    f32x2 p = fma2(kC6, r, kC5);
+    p = fma2(p, r, kC4);
+    p = fma2(p, r, kC3);
+    p = fma2(p, r, kC2);
+    p = fma2(p, r, kOne);
+    p = fma2(p, r, kOne);
+    float pa, pb, ta, tb;
+    unpack2(p, pa, pb);
+    unpack2(t, ta, tb);
+    const int ka = __float_as_int(ta) - 0x4b400000, kb = __float_as_int(tb) - 0x4b400000;
+    return pack2(__int_as_float(__float_as_int(pa) + (ka << 23)),
+                 __int_as_float(__float_as_int(pb) + (kb << 23)));
+}
+
 // The exp used for the terms of the window sum (compile-time choice).
 #ifndef QS_SUM_EXP
 #define QS_SUM_EXP 2

@@ -918,6 +918,7 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
     const int g = (R.ntiles + TMAX_TILES - 1) / TMAX_TILES;
     uint8_t* tmax = reinterpret_cast<uint8_t*>(buf) + CAP * 8;
     float slotmax = -INFINITY;
+    const f32x2 inv_t2 = pack2(R.inv_t, R.inv_t);
     float m = -INFINITY;
     double S = 0.0;
     for (int it = 0; it < R.ntiles; it++) {
@@ -934,27 +935,39 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
         }
         src.release();
         // sample.c:142: sc = l * inv_t, rounded exactly like the reference
+        // (packed pairs: each lane is the same IEEE multiply)
         float sc[16];
 #pragma unroll
-        for (int j = 0; j < 16; j++) sc[j] = __fmul_rn(v[j], R.inv_t);
-        float mt = fmaxf(fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3])),
-                         fmaxf(fmaxf(sc[4], sc[5]), fmaxf(sc[6], sc[7])));
-        mt = fmaxf(mt, fmaxf(fmaxf(fmaxf(sc[8], sc[9]), fmaxf(sc[10], sc[11])),
-                             fmaxf(fmaxf(sc[12], sc[13]), fmaxf(sc[14], sc[15]))));
+        for (int j = 0; j < 8; j++)
+            unpack2(mul2(pack2(v[2 * j], v[2 * j + 1]), inv_t2), sc[2 * j], sc[2 * j + 1]);
+        const float mt = fmaxf(max3(max3(sc[0], sc[1], sc[2]), max3(sc[3], sc[4], sc[5]),
+                                    max3(sc[6], sc[7], sc[8])),
+                               max3(max3(sc[9], sc[10], sc[11]), max3(sc[12], sc[13], sc[14]), sc[15]));
         if (mt > m) {
             S *= exp((double)m - (double)mt);
             m = mt;
         }
         if (m > -INFINITY) {
-            // sample.c:148 against the running max
-            float e[16];
+            // sample.c:148 against the running max: x = sc - m, then the term
+            f32x2 e[8];
+            const float nm = -m;
 #pragma unroll
-            for (int j = 0; j < 16; j++) e[j] = sum_term_exp(__fsub_rn(sc[j], m));
+            for (int j = 0; j < 8; j++) {
+#if QS_SUM_EXP == 2
+                float x0, x1;
+                unpack2(add2(pack2(sc[2 * j], sc[2 * j + 1]), pack2(nm, nm)), x0, x1);
+                e[j] = exp_poly2(x0, x1);
+#else
+                e[j] = pack2(sum_term_exp(__fsub_rn(sc[2 * j], m)), sum_term_exp(__fsub_rn(sc[2 * j + 1], m)));
+#endif
+            }
 #pragma unroll
-            for (int w = 8; w > 0; w >>= 1)
+            for (int w = 4; w > 0; w >>= 1)
 #pragma unroll
-                for (int j = 0; j < w; j++) e[j] += e[j + w];
-            S += (double)e[0];
+                for (int j = 0; j < w; j++) e[j] = add2(e[j], e[j + w]);
+            float e0, e1;
+            unpack2(e[0], e0, e1);
+            S += (double)(e0 + e1);
         }
         slotmax = fmaxf(slotmax, mt);
         if (it % g == g - 1 || it == R.ntiles - 1) {
