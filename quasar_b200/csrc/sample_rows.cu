@@ -65,9 +65,8 @@ struct Hist {
     unsigned long long mass2[NB];
     int32_t minid2[NB];
 };
-// candidate keys [CAP] followed by the tile-max table (main kernels); the
-// select kernel keeps its histograms in a layout of its own
-constexpr int SCRATCH_BYTES = CAP * 8 + TMAX_BYTES;
+// kernel B scratch: candidate keys [CAP]; the select path's histograms alias it
+constexpr int FINISH_SCRATCH = (int)sizeof(Hist) > CAP * 8 ? (int)sizeof(Hist) : CAP * 8;
 
 struct Shared {
     int abort;            // a bounded wait gave up
@@ -766,7 +765,7 @@ struct RowCtx {
     const int32_t* ring;
 };
 
-// Row parameters, history ring and the penalty bitset of `row`.
+// Row parameters, history ring and (with_bits) the penalty bitset of `row`.
 __device__ __forceinline__ RowCtx row_setup(const RowsArgs& a, int row, Row& R, uint32_t* bits) {
     const int tid = threadIdx.x;
     RowCtx c;
@@ -840,12 +839,11 @@ __device__ __forceinline__ void row_finish(const RowsArgs& a, int row, const Row
 }
 
 // ---------------------------------------------------------------------------
-// One row, all consumer threads. Greedy and candidate-path rows are finished
-// here; a row the candidate path cannot bound is handed to the select kernel
-// (its id, report, PRNG step and ring append are written there).
+// Kernel A, one row: greedy rows are finished here; a stochastic row is
+// streamed once and leaves its summary in the workspace (max M, 1/sum, the
+// per-thread maxima and the tile-max table) for kernel B.
 template <class Src>
-__device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src, uint64_t* buf,
-                                            uint32_t* bits, Shared& s) {
+__device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src, uint32_t* bits, Shared& s) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint8_t* bits8 = reinterpret_cast<const uint8_t*>(bits);
     Row R;
@@ -853,8 +851,6 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
     const RowParams& P = c.P;
     src.begin(R);
 
-    int path = QUASAR_PATH_GREEDY;
-    uint64_t st_rng = 0;
     if (P.T <= 0.0f) {
         // ---- greedy: penalized argmax, first index on ties ----
         float bv = -INFINITY;
@@ -909,14 +905,13 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
             s.res_p = 1.0f;
         }
         csync();
-        row_finish(a, row, c, R, bits, path, st_rng, s);
+        row_finish(a, row, c, R, bits, QUASAR_PATH_GREEDY, 0, s);
         return;
     }
 
     // ---- one streaming pass: max, online window sum, tile maxima ----
-    // slots of the tile-max table: one per thread and group of g tiles
-    const int g = (R.ntiles + TMAX_TILES - 1) / TMAX_TILES;
-    uint8_t* tmax = reinterpret_cast<uint8_t*>(buf) + CAP * 8;
+    const int g = (R.ntiles + TMAX_TILES - 1) / TMAX_TILES;  // tiles per table slot
+    uint8_t* tmax = a.work_tmax + (int64_t)row * TMAX_BYTES;
     float slotmax = -INFINITY;
     const f32x2 inv_t2 = pack2(R.inv_t, R.inv_t);
     float m = -INFINITY;
@@ -975,21 +970,50 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
             slotmax = -INFINITY;
         }
     }
-    s.tfmax[tid] = m;
-    R.M = block_max_f(m, s);
-    const double contrib = (m > -INFINITY) ? S * exp((double)m - (double)R.M) : 0.0;
+    a.work_tfmax[(int64_t)row * CONSUMERS + tid] = m;
+    const float M = block_max_f(m, s);
+    const double contrib = (m > -INFINITY) ? S * exp((double)m - (double)M) : 0.0;
     const double Stot = block_sum_d(contrib, s);
-    R.inv = __double2float_rn(1.0 / Stot);
-    R.thr = __fsub_rn(R.M, 30.0f);
+    if (tid == 0) a.work_info[row] = make_float2(M, __double2float_rn(1.0 / Stot));
+    clear_bits(a, c, R, bits);
+    csync();
+}
 
-    // Candidate path. The kept prefix lies above a threshold known once M is:
-    // min_p -> sc >= M + ln(min_p) - 0.01 (every p >= min_p * p_max clears
-    // it); top_k -> the k-th largest per-thread max less a tie margin (k
-    // distinct elements reach it). Only thread-tiles whose bound clears the
-    // threshold are read again.
+// ---------------------------------------------------------------------------
+// Kernel B, one stochastic row: cuts and draw from the row summary.
+//
+// Candidate path. The kept prefix lies above a threshold known once M is:
+// min_p -> sc >= M + ln(min_p) - 0.01 (every p >= min_p * p_max clears it);
+// top_k -> the k-th largest per-thread max less a tie margin (k distinct
+// elements reach it). Only thread-tiles whose bound clears the threshold are
+// read again. Rows it cannot bound take the exact select path.
+__device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t* buf, uint32_t* bits,
+                                           Shared& s) {
+    const int tid = threadIdx.x, lane = tid & 31;
+    const uint8_t* bits8 = reinterpret_cast<const uint8_t*>(bits);
+    {
+        const quasar_sample_params pr = a.d_params ? a.d_params[row] : a.h_params;
+        if (!(pr.temperature > 0.0f)) return;  // greedy: finished by kernel A
+    }
+    Row R;
+    const RowCtx c = row_setup(a, row, R, bits);
+    const RowParams& P = c.P;
+    const float2 info = a.work_info[row];
+    R.M = info.x;
+    R.inv = info.y;
+    R.thr = __fsub_rn(R.M, 30.0f);
+    const float m = a.work_tfmax[(int64_t)row * CONSUMERS + tid];  // this thread's max in kernel A
+    s.tfmax[tid] = m;
+    const uint8_t* tmax = a.work_tmax + (int64_t)row * TMAX_BYTES;
+    const int g = (R.ntiles + TMAX_TILES - 1) / TMAX_TILES;
+    csync();
+
+    uint64_t st_rng = a.rng[row];
+    const double u = rng_unit(&st_rng);  // sample.c:173: one step per stochastic row
+    int path = QUASAR_PATH_SELECT;
+    bool done = false;
     const bool by_minp = P.min_p > 0.0f;
     const bool by_topk = P.top_k > 0 && P.top_k <= TOPK_MAX;
-    bool done = false;
     if (!(a.flags & QUASAR_FLAG_EXACT_SELECT) && (by_minp || by_topk)) {
         const int nslot = ((R.ntiles + g - 1) / g) * CONSUMERS;
         float tau = -INFINITY;
@@ -1079,8 +1103,6 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
                 bitonic_desc(area, n2);
                 keys = area;
             }
-            st_rng = a.rng[row];
-            const double u = rng_unit(&st_rng);  // sample.c:173: one step per stochastic row
             candidate_cuts(keys, nk, P, by_minp ? __fmul_rn(P.min_p, R.inv) : 0.0f, u, s);
             done = true;
             path = QUASAR_PATH_CANDIDATE;
@@ -1088,44 +1110,33 @@ __device__ __forceinline__ void process_row(const RowsArgs& a, int row, Src& src
         csync();
     }
     if (!done) {
-        // the exact select path runs in sample_rows_select over the listed rows
-        if (tid == 0) {
-            const int i = atomicAdd(a.work_count, 1);
-            a.work_rows[i] = row;
-            a.work_M[i] = R.M;
-            a.work_inv[i] = R.inv;
-        }
-        clear_bits(a, c, R, bits);
         csync();
-        return;
+        select_path(R, bits8, reinterpret_cast<Hist*>(buf), P, u, s);
     }
     row_finish(a, row, c, R, bits, path, st_rng, s);
 }
 
 // ---------------------------------------------------------------------------
-// Dynamic shared memory of the LDG kernel: [scratch][bits]; of the TMA kernel:
-// [ring NSTAGE x 16 KB][scratch][bits][full bars][empty bars]; of the select
-// kernel: [Hist][bits].
+// Kernels. Dynamic shared memory: kernel A row-load variant [bits]; kernel A
+// ring variant [ring NSTAGE x 16 KB][bits][full bars][empty bars]; kernel B
+// [scratch: candidate keys / select histograms][bits].
 
-__global__ void __launch_bounds__(CONSUMERS, 3) sample_rows_ldg(RowsArgs a) {
+__global__ void __launch_bounds__(CONSUMERS, 4) sample_rows_ldg(RowsArgs a) {
     extern __shared__ __align__(128) unsigned char dyn[];
-    uint64_t* buf = reinterpret_cast<uint64_t*>(dyn);
-    uint32_t* bits = reinterpret_cast<uint32_t*>(dyn + SCRATCH_BYTES);
+    uint32_t* bits = reinterpret_cast<uint32_t*>(dyn);
     __shared__ Shared s;
     for (int i = threadIdx.x; i < a.nwords; i += CONSUMERS) bits[i] = 0u;
     if (threadIdx.x == 0) s.abort = 0;
     csync();
     LdgSource src;
-    for (int row = blockIdx.x; row < a.B; row += gridDim.x) process_row(a, row, src, buf, bits, s);
+    for (int row = blockIdx.x; row < a.B; row += gridDim.x) stream_row(a, row, src, bits, s);
 }
 
-__global__ void __launch_bounds__(CONSUMERS + 32, 2) sample_rows_tma(RowsArgs a) {
+__global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a) {
     extern __shared__ __align__(128) unsigned char dyn[];
     float* ring = reinterpret_cast<float*>(dyn);
-    uint64_t* buf = reinterpret_cast<uint64_t*>(dyn + NSTAGE * TILE_BYTES);
-    uint32_t* bits = reinterpret_cast<uint32_t*>(dyn + NSTAGE * TILE_BYTES + SCRATCH_BYTES);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(dyn + NSTAGE * TILE_BYTES + SCRATCH_BYTES +
-                                                 ((a.nwords * 4 + 7) & ~7));
+    uint32_t* bits = reinterpret_cast<uint32_t*>(dyn + NSTAGE * TILE_BYTES);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(dyn + NSTAGE * TILE_BYTES + ((a.nwords * 4 + 7) & ~7));
     __shared__ Shared s;
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + NSTAGE);
     if (threadIdx.x == 0) {
@@ -1169,10 +1180,12 @@ __global__ void __launch_bounds__(CONSUMERS + 32, 2) sample_rows_tma(RowsArgs a)
     src.full0 = full0;
     src.empty0 = empty0;
     src.g = 0;
-    for (int row = blockIdx.x; row < a.B; row += gridDim.x) process_row(a, row, src, buf, bits, s);
+    for (int row = blockIdx.x; row < a.B; row += gridDim.x) stream_row(a, row, src, bits, s);
     // After an abort, give chunks still in flight a bounded chance to land
-    // before the CTA (and its shared memory) goes away.
+    // before the CTA (and its shared memory) goes away; the rows of this CTA
+    // are marked failed (id -1) by kernel B through the abort word.
     if (threadIdx.x == 0 && *reinterpret_cast<volatile int*>(&s.abort)) {
+        atomicExch(a.work_abort, 1);
         for (int k = 1; k <= NSTAGE && (uint32_t)k <= src.g; k++) {
             const uint32_t g = src.g - k;
             mbar_wait(full0 + 8u * (g % NSTAGE), (g / NSTAGE) & 1u);
@@ -1180,53 +1193,37 @@ __global__ void __launch_bounds__(CONSUMERS + 32, 2) sample_rows_tma(RowsArgs a)
     }
 }
 
-// Rows the candidate path handed over: exact radix select over the whole row
-// (re-reading it), then the row's outputs. Runs after the main kernel on the
-// same stream, so the list is complete; with no listed row it exits at once.
-__global__ void __launch_bounds__(CONSUMERS) sample_rows_select(RowsArgs a) {
+__global__ void __launch_bounds__(CONSUMERS) sample_rows_finish(RowsArgs a) {
     extern __shared__ __align__(128) unsigned char dyn[];
-    Hist* H = reinterpret_cast<Hist*>(dyn);
-    uint32_t* bits = reinterpret_cast<uint32_t*>(dyn + sizeof(Hist));
-    const uint8_t* bits8 = reinterpret_cast<const uint8_t*>(bits);
+    uint64_t* buf = reinterpret_cast<uint64_t*>(dyn);
+    uint32_t* bits = reinterpret_cast<uint32_t*>(dyn + FINISH_SCRATCH);
     __shared__ Shared s;
-    const int n = *a.work_count;
-    if ((int)blockIdx.x >= n) return;
     for (int i = threadIdx.x; i < a.nwords; i += CONSUMERS) bits[i] = 0u;
-    if (threadIdx.x == 0) s.abort = 0;
+    if (threadIdx.x == 0) s.abort = *reinterpret_cast<volatile int*>(a.work_abort);
     csync();
-    for (int i = blockIdx.x; i < n; i += gridDim.x) {
-        const int row = a.work_rows[i];
-        Row R;
-        const RowCtx c = row_setup(a, row, R, bits);
-        R.M = a.work_M[i];
-        R.inv = a.work_inv[i];
-        R.thr = __fsub_rn(R.M, 30.0f);
-        uint64_t st = a.rng[row];
-        const double u = rng_unit(&st);  // sample.c:173
-        select_path(R, bits8, H, c.P, u, s);
-        row_finish(a, row, c, R, bits, QUASAR_PATH_SELECT, st, s);
-    }
+    for (int row = blockIdx.x; row < a.B; row += gridDim.x) finish_row(a, row, buf, bits, s);
 }
 
 }  // namespace rows
 
 static int nwords_for(int V) { return ((V + 31) >> 5) + 1; }
 
-size_t rows_smem_bytes(int V) {  // LDG kernel
-    return (size_t)rows::SCRATCH_BYTES + (size_t)nwords_for(V) * sizeof(uint32_t);
+size_t rows_smem_bytes(int V) {  // kernel A, row-load variant
+    return (size_t)nwords_for(V) * sizeof(uint32_t);
 }
 
-size_t rows_tma_smem_bytes(int V) {
-    return (size_t)rows::NSTAGE * rows::TILE_BYTES + rows::SCRATCH_BYTES +
-           (((size_t)nwords_for(V) * 4 + 7) & ~(size_t)7) + 2 * rows::NSTAGE * sizeof(uint64_t);
+size_t rows_tma_smem_bytes(int V) {  // kernel A, ring variant
+    return (size_t)rows::NSTAGE * rows::TILE_BYTES + (((size_t)nwords_for(V) * 4 + 7) & ~(size_t)7) +
+           2 * rows::NSTAGE * sizeof(uint64_t);
 }
 
-size_t rows_select_smem_bytes(int V) {
-    return sizeof(rows::Hist) + (size_t)nwords_for(V) * sizeof(uint32_t);
+size_t rows_finish_smem_bytes(int V) {  // kernel B
+    return (size_t)rows::FINISH_SCRATCH + (size_t)nwords_for(V) * sizeof(uint32_t);
 }
 
+// [abort word][pad][info B x float2][tfmax B x 256 floats][tmax B x TMAX_BYTES]
 size_t rows_workspace_bytes(int B) {
-    return (size_t)256 + (size_t)B * 12 + 256;
+    return (size_t)256 + (size_t)B * (8 + 4 * rows::CONSUMERS + rows::TMAX_BYTES);
 }
 
 int rows_threads() { return rows::CONSUMERS; }
@@ -1234,9 +1231,9 @@ int rows_threads() { return rows::CONSUMERS; }
 namespace {
 struct KernelCfg {
     size_t smem_set[64];
-    int grid[64];  // persistent grid of the kernel on each device
+    int grid[64];  // resident CTAs of the kernel on each device
 };
-thread_local KernelCfg g_ldg = {}, g_tma = {}, g_sel = {};
+thread_local KernelCfg g_ldg = {}, g_tma = {}, g_fin = {};
 
 cudaError_t configure(KernelCfg& cfg, const void* fn, int threads, size_t smem, int dev) {
     cudaError_t err = cudaSuccess;
@@ -1261,17 +1258,16 @@ cudaError_t configure(KernelCfg& cfg, const void* fn, int threads, size_t smem, 
 cudaError_t launch_sample_rows(const RowsArgs& args, void* workspace, cudaStream_t stream) {
     RowsArgs a = args;
     a.nwords = nwords_for(args.V);
-    // workspace: [count][pad][rows B][M B][inv B]
     char* ws = reinterpret_cast<char*>(workspace);
-    a.work_count = reinterpret_cast<int*>(ws);
-    a.work_rows = reinterpret_cast<int*>(ws + 256);
-    a.work_M = reinterpret_cast<float*>(ws + 256 + (size_t)args.B * 4);
-    a.work_inv = reinterpret_cast<float*>(ws + 256 + (size_t)args.B * 8);
+    a.work_abort = reinterpret_cast<int*>(ws);
+    a.work_info = reinterpret_cast<float2*>(ws + 256);
+    a.work_tfmax = reinterpret_cast<float*>(ws + 256 + (size_t)args.B * 8);
+    a.work_tmax = reinterpret_cast<uint8_t*>(ws + 256 + (size_t)args.B * (8 + 4 * rows::CONSUMERS));
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
     if (err != cudaSuccess) return err;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    err = cudaMemsetAsync(a.work_count, 0, sizeof(int), stream);
+    err = cudaMemsetAsync(a.work_abort, 0, sizeof(int), stream);
     if (err != cudaSuccess) return err;
     if (a.tma) {
         const size_t smem = rows_tma_smem_bytes(a.V);
@@ -1282,14 +1278,14 @@ cudaError_t launch_sample_rows(const RowsArgs& args, void* workspace, cudaStream
         const size_t smem = rows_smem_bytes(a.V);
         err = configure(g_ldg, (const void*)rows::sample_rows_ldg, rows::CONSUMERS, smem, dev);
         if (err != cudaSuccess) return err;
-        rows::sample_rows_ldg<<<a.B, rows::CONSUMERS, smem, stream>>>(a);
+        rows::sample_rows_ldg<<<min(a.B, g_ldg.grid[dev]), rows::CONSUMERS, smem, stream>>>(a);
     }
     err = cudaGetLastError();
     if (err != cudaSuccess) return err;
-    const size_t ssmem = rows_select_smem_bytes(a.V);
-    err = configure(g_sel, (const void*)rows::sample_rows_select, rows::CONSUMERS, ssmem, dev);
+    const size_t fsmem = rows_finish_smem_bytes(a.V);
+    err = configure(g_fin, (const void*)rows::sample_rows_finish, rows::CONSUMERS, fsmem, dev);
     if (err != cudaSuccess) return err;
-    rows::sample_rows_select<<<min(a.B, g_sel.grid[dev]), rows::CONSUMERS, ssmem, stream>>>(a);
+    rows::sample_rows_finish<<<a.B, rows::CONSUMERS, fsmem, stream>>>(a);
     return cudaGetLastError();
 }
 

@@ -27,19 +27,19 @@ struct RowsArgs {
     int vec;     // rows 32-byte aligned with ld % 8 == 0 (256-bit global loads)
     int tma;     // rows 16-byte aligned, ld % 4 == 0, V % 4 == 0 (bulk-copy ring kernel)
     int nwords;  // bitset words (set by the launcher)
-    // rows handed to the select kernel (workspace; set by the launcher)
-    int* work_count;
-    int* work_rows;
-    float* work_M;
-    float* work_inv;
+    // per-row summaries kernel A leaves for kernel B (workspace; set by the launcher)
+    int* work_abort;
+    float2* work_info;      // (max scaled logit, 1/sum)
+    float* work_tfmax;      // [B][256] per-thread running maxima
+    uint8_t* work_tmax;     // [B][TMAX] tile-max deficits
 };
 
 size_t rows_smem_bytes(int V);      // one-CTA-per-row kernel
 size_t rows_tma_smem_bytes(int V);  // persistent bulk-copy ring kernel
-size_t rows_select_smem_bytes(int V);
+size_t rows_finish_smem_bytes(int V);
 size_t rows_workspace_bytes(int B);  // device workspace of one launch
 int rows_threads();
-// Zeroes the workspace counter, launches the main kernel and the select kernel.
+// Launches kernel A (one streaming pass per row) and kernel B (cuts and draw).
 cudaError_t launch_sample_rows(const RowsArgs& args, void* workspace, cudaStream_t stream);
 
 }  // namespace qs
