@@ -56,6 +56,13 @@ constexpr int TOPK_MAX = CONSUMERS;            // largest top_k the candidate pa
 constexpr int QMAX = 4096;                     // qualifying thread-tiles re-read per row
 constexpr int NB = 1024;                       // radix bins per level (10 bits)
 constexpr long long WAIT_CYCLES = 1ll << 32;   // ~2 s: bound on any mbarrier wait
+#ifndef QS_LDG_DEPTH
+#define QS_LDG_DEPTH 1
+#endif
+#ifndef QS_A_CTAS
+#define QS_A_CTAS 4
+#endif
+constexpr int LDG_DEPTH = QS_LDG_DEPTH;        // tiles in flight per thread, row-load kernel
 
 // The select path reuses the candidate storage as histograms.
 struct Hist {
@@ -149,6 +156,20 @@ __device__ __forceinline__ void load_oct(const float* row, int o, int V, bool ve
     } else {
 #pragma unroll
         for (int k = 0; k < 8; k++) v[k] = (e + k < V) ? __ldcs(row + e + k) : -INFINITY;
+    }
+}
+
+// The same octet load with the default cache policy (re-reads of a few tiles).
+__device__ __forceinline__ void load_oct_keep(const float* row, int o, int V, bool vec, float* v) {
+    const int e = o * 8;
+    if (vec && e + 7 < V) {
+        asm volatile("ld.global.nc.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                     : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]),
+                       "=f"(v[6]), "=f"(v[7])
+                     : "l"(row + e));
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = (e + k < V) ? __ldg(row + e + k) : -INFINITY;
     }
 }
 
@@ -700,18 +721,26 @@ __device__ float topk_floor(int k, Shared& s) {
 // it*OCT_TILE + 256 + tid (index order within a thread is kept).
 
 struct LdgSource {
-    float nxt[16];
-    __device__ __forceinline__ void begin(const Row& R) { load(R, 0, nxt); }
+    float nxt[LDG_DEPTH][16];  // tiles it+1 .. it+LDG_DEPTH in flight
+    __device__ __forceinline__ void begin(const Row& R) {
+#pragma unroll
+        for (int d = 0; d < LDG_DEPTH; d++)
+            if (d < R.ntiles) load(R, d, nxt[d]);
+    }
     __device__ __forceinline__ static void load(const Row& R, int it, float* v) {
         const int o0 = it * OCT_TILE + threadIdx.x;
         load_oct(R.ptr, o0, R.V, R.vec, v);
         load_oct(R.ptr, o0 + CONSUMERS, R.V, R.vec, v + 8);
     }
-    // tile `it` into v; the next tile's loads are issued before returning
+    // tile `it` into v; the loads of tile it+LDG_DEPTH are issued before returning
     __device__ __forceinline__ void get(const Row& R, int it, float (&v)[16], Shared&) {
 #pragma unroll
-        for (int j = 0; j < 16; j++) v[j] = nxt[j];
-        if (it + 1 < R.ntiles) load(R, it + 1, nxt);
+        for (int j = 0; j < 16; j++) v[j] = nxt[0][j];
+#pragma unroll
+        for (int d = 0; d + 1 < LDG_DEPTH; d++)
+#pragma unroll
+            for (int j = 0; j < 16; j++) nxt[d][j] = nxt[d + 1][j];
+        if (it + LDG_DEPTH < R.ntiles) load(R, it + LDG_DEPTH, nxt[LDG_DEPTH - 1]);
     }
     __device__ __forceinline__ void release() {}
 };
@@ -1029,10 +1058,18 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
         // re-reads spread over all threads and issue in one round; raw
         // survivors are appended from the top of buf downwards
         uint32_t* qlist = reinterpret_cast<uint32_t*>(buf);
-        for (int sl = 0; sl * CONSUMERS < nslot; sl++) {
-            if (tile_bound(m, tmax[sl * CONSUMERS + tid]) >= lo) {
-                const int q = atomicAdd(&s.nq, 1);
-                if (q < QMAX) qlist[q] = (uint32_t)(sl * CONSUMERS + tid);
+        {
+            // this thread's table entries, all loads in flight at once
+            const int nsl = nslot / CONSUMERS;
+            uint32_t d[TMAX_TILES];
+#pragma unroll
+            for (int sl = 0; sl < TMAX_TILES; sl++) d[sl] = sl < nsl ? tmax[sl * CONSUMERS + tid] : 255u;
+#pragma unroll
+            for (int sl = 0; sl < TMAX_TILES; sl++) {
+                if (sl < nsl && tile_bound(m, (uint8_t)d[sl]) >= lo) {
+                    const int q = atomicAdd(&s.nq, 1);
+                    if (q < QMAX) qlist[q] = (uint32_t)(sl * CONSUMERS + tid);
+                }
             }
         }
         csync();
@@ -1050,8 +1087,8 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
                 float sc[16];
                 uint32_t mask = 0u;
                 if (ok) {
-                    load_oct(R.ptr, o0, R.V, R.vec, sc);
-                    load_oct(R.ptr, o1, R.V, R.vec, sc + 8);
+                    load_oct_keep(R.ptr, o0, R.V, R.vec, sc);
+                    load_oct_keep(R.ptr, o1, R.V, R.vec, sc + 8);
                     if (R.use_pen) {
                         apply_pen_oct(sc, o0 < R.noct ? bits8[o0] : 0u, R.rp);
                         apply_pen_oct(sc + 8, o1 < R.noct ? bits8[o1] : 0u, R.rp);
@@ -1121,7 +1158,7 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
 // ring variant [ring NSTAGE x 16 KB][bits][full bars][empty bars]; kernel B
 // [scratch: candidate keys / select histograms][bits].
 
-__global__ void __launch_bounds__(CONSUMERS, 4) sample_rows_ldg(RowsArgs a) {
+__global__ void __launch_bounds__(CONSUMERS, QS_A_CTAS) sample_rows_ldg(RowsArgs a) {
     extern __shared__ __align__(128) unsigned char dyn[];
     uint32_t* bits = reinterpret_cast<uint32_t*>(dyn);
     __shared__ Shared s;
@@ -1193,7 +1230,7 @@ __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a)
     }
 }
 
-__global__ void __launch_bounds__(CONSUMERS) sample_rows_finish(RowsArgs a) {
+__global__ void __launch_bounds__(CONSUMERS, 3) sample_rows_finish(RowsArgs a) {
     extern __shared__ __align__(128) unsigned char dyn[];
     uint64_t* buf = reinterpret_cast<uint64_t*>(dyn);
     uint32_t* bits = reinterpret_cast<uint32_t*>(dyn + FINISH_SCRATCH);
