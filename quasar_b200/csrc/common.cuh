@@ -91,8 +91,8 @@ __device__ __forceinline__ float exp_poly(float x) {
     p = __fmaf_rn(p, r, 0.49999991059303284f);
     p = __fmaf_rn(p, r, 1.0f);
     p = __fmaf_rn(p, r, 1.0f);
-    const int k = __float_as_int(t) - __float_as_int(kMagic);
-    return __int_as_float(__float_as_int(p) + (k << 23));
+    // bits(t) = bits(kMagic) + k and bits(kMagic) << 23 == 0 (mod 2^32)
+    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 // ---- packed fp32x2 arithmetic (sm_100: one instruction for two lanes, each
@@ -150,9 +150,10 @@ __device__ __forceinline__ f32x2 exp_poly2(float a, float b) {
     float pa, pb, ta, tb;
     unpack2(p, pa, pb);
     unpack2(t, ta, tb);
-    const int ka = __float_as_int(ta) - 0x4b400000, kb = __float_as_int(tb) - 0x4b400000;
-    return pack2(__int_as_float(__float_as_int(pa) + (ka << 23)),
-                 __int_as_float(__float_as_int(pb) + (kb << 23)));
+    // bits(t) = 0x4b400000 + k and 0x4b400000 << 23 == 0 (mod 2^32), so
+    // bits(t) << 23 == k << 23: the exponent step of 2^k in one shift
+    return pack2(__int_as_float(__float_as_int(pa) + (__float_as_int(ta) << 23)),
+                 __int_as_float(__float_as_int(pb) + (__float_as_int(tb) << 23)));
 }
 
 // The exp used for the terms of the window sum (compile-time choice).

@@ -143,6 +143,14 @@ __device__ __forceinline__ unsigned long long fixp(uint32_t pkey) {
     return __float2ull_rz(__fmul_rn(__uint_as_float(pkey), 4611686018427387904.0f));
 }
 
+// 256-bit streaming load of 8 floats (32-byte aligned address).
+__device__ __forceinline__ void ld8(const float* p, float* v) {
+    asm volatile("ld.global.nc.L1::no_allocate.L2::evict_first.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]),
+                   "=f"(v[7])
+                 : "l"(p));
+}
+
 // One 32-byte octet of a row (elements 8o..8o+7) from global memory: a single
 // 256-bit load when the row is 32-byte aligned (sm_100 ld.global.v8), else
 // masked scalar loads; elements past V read as -inf.
@@ -721,6 +729,7 @@ __device__ float topk_floor(int k, Shared& s) {
 // it*OCT_TILE + 256 + tid (index order within a thread is kept).
 
 struct LdgSource {
+    static constexpr bool kRegs = true;
     float nxt[LDG_DEPTH][16];  // tiles it+1 .. it+LDG_DEPTH in flight
     __device__ __forceinline__ void begin(const Row& R) {
 #pragma unroll
@@ -729,8 +738,13 @@ struct LdgSource {
     }
     __device__ __forceinline__ static void load(const Row& R, int it, float* v) {
         const int o0 = it * OCT_TILE + threadIdx.x;
-        load_oct(R.ptr, o0, R.V, R.vec, v);
-        load_oct(R.ptr, o0 + CONSUMERS, R.V, R.vec, v + 8);
+        if (R.vec && it + 1 < R.ntiles) {  // a full tile of a 32-byte aligned row
+            ld8(R.ptr + 8 * o0, v);
+            ld8(R.ptr + 8 * (o0 + CONSUMERS), v + 8);
+        } else {
+            load_oct(R.ptr, o0, R.V, R.vec, v);
+            load_oct(R.ptr, o0 + CONSUMERS, R.V, R.vec, v + 8);
+        }
     }
     // tile `it` into v; the loads of tile it+LDG_DEPTH are issued before returning
     __device__ __forceinline__ void get(const Row& R, int it, float (&v)[16], Shared&) {
@@ -746,6 +760,7 @@ struct LdgSource {
 };
 
 struct TmaSource {
+    static constexpr bool kRegs = false;
     const float* ring;  // NSTAGE tiles
     uint32_t full0, empty0;
     uint32_t g;  // chunks consumed by this CTA so far
@@ -867,6 +882,31 @@ __device__ __forceinline__ void row_finish(const RowsArgs& a, int row, const Row
     csync();
 }
 
+// Runs body(v, it) over every tile of the row. Register loads: two buffers
+// alternate, the next tile's loads in flight while one is processed, with
+// unchecked 256-bit loads for every tile but the last. Ring: tiles come from
+// shared memory and the stage is released as soon as it is in registers.
+template <class Src, class F>
+__device__ __forceinline__ void stream_tiles(const Row& R, Src& src, Shared& s, F& body) {
+    if constexpr (Src::kRegs) {
+        float va[16], vb[16];
+        Src::load(R, 0, va);
+        for (int it = 0; it < R.ntiles; it += 2) {
+            if (it + 1 < R.ntiles) Src::load(R, it + 1, vb);
+            body(va, it);
+            if (it + 2 < R.ntiles) Src::load(R, it + 2, va);
+            if (it + 1 < R.ntiles) body(vb, it + 1);
+        }
+    } else {
+        for (int it = 0; it < R.ntiles; it++) {
+            float v[16];
+            src.get(R, it, v, s);
+            src.release();
+            body(v, it);
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Kernel A, one row: greedy rows are finished here; a stochastic row is
 // streamed once and leaves its summary in the workspace (max M, 1/sum, the
@@ -945,9 +985,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
     const f32x2 inv_t2 = pack2(R.inv_t, R.inv_t);
     float m = -INFINITY;
     double S = 0.0;
-    for (int it = 0; it < R.ntiles; it++) {
-        float v[16];
-        src.get(R, it, v, s);
+    auto body = [&](float (&v)[16], int it) {
         const int o0 = it * OCT_TILE + tid, o1 = o0 + CONSUMERS;
         if (R.use_pen) {
             const uint32_t m0 = o0 < R.noct ? bits8[o0] : 0u;
@@ -957,13 +995,15 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
                 apply_pen_oct(v + 8, m1, R.rp);
             }
         }
-        src.release();
         // sample.c:142: sc = l * inv_t, rounded exactly like the reference
         // (packed pairs: each lane is the same IEEE multiply)
+        f32x2 sc2[8];
         float sc[16];
 #pragma unroll
-        for (int j = 0; j < 8; j++)
-            unpack2(mul2(pack2(v[2 * j], v[2 * j + 1]), inv_t2), sc[2 * j], sc[2 * j + 1]);
+        for (int j = 0; j < 8; j++) {
+            sc2[j] = mul2(pack2(v[2 * j], v[2 * j + 1]), inv_t2);
+            unpack2(sc2[j], sc[2 * j], sc[2 * j + 1]);
+        }
         const float mt = fmaxf(max3(max3(sc[0], sc[1], sc[2]), max3(sc[3], sc[4], sc[5]),
                                     max3(sc[6], sc[7], sc[8])),
                                max3(max3(sc[9], sc[10], sc[11]), max3(sc[12], sc[13], sc[14]), sc[15]));
@@ -974,12 +1014,12 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
         if (m > -INFINITY) {
             // sample.c:148 against the running max: x = sc - m, then the term
             f32x2 e[8];
-            const float nm = -m;
+            const f32x2 nm2 = pack2(-m, -m);
 #pragma unroll
             for (int j = 0; j < 8; j++) {
 #if QS_SUM_EXP == 2
                 float x0, x1;
-                unpack2(add2(pack2(sc[2 * j], sc[2 * j + 1]), pack2(nm, nm)), x0, x1);
+                unpack2(add2(sc2[j], nm2), x0, x1);
                 e[j] = exp_poly2(x0, x1);
 #else
                 e[j] = pack2(sum_term_exp(__fsub_rn(sc[2 * j], m)), sum_term_exp(__fsub_rn(sc[2 * j + 1], m)));
@@ -993,12 +1033,17 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
             unpack2(e[0], e0, e1);
             S += (double)(e0 + e1);
         }
-        slotmax = fmaxf(slotmax, mt);
-        if (it % g == g - 1 || it == R.ntiles - 1) {
-            tmax[(it / g) * CONSUMERS + tid] = tile_deficit(m, slotmax);
-            slotmax = -INFINITY;
+        if (g == 1) {
+            tmax[it * CONSUMERS + tid] = tile_deficit(m, mt);
+        } else {
+            slotmax = fmaxf(slotmax, mt);
+            if (it % g == g - 1 || it == R.ntiles - 1) {
+                tmax[(it / g) * CONSUMERS + tid] = tile_deficit(m, slotmax);
+                slotmax = -INFINITY;
+            }
         }
-    }
+    };
+    stream_tiles(R, src, s, body);
     a.work_tfmax[(int64_t)row * CONSUMERS + tid] = m;
     const float M = block_max_f(m, s);
     const double contrib = (m > -INFINITY) ? S * exp((double)m - (double)M) : 0.0;
