@@ -169,7 +169,8 @@ int quasar_synth_uniform(uint64_t seed, int64_t row0, int B, float lo, float hi,
 
 /* Evaluates one of the sampler's exp variants on d_x[n] into d_out[n]:
  * which = 0 ex2.approx with a split argument, 1 CUDA expf, 2 a correctly
- * rounded (float)exp((double)x), 3 the FMA-polynomial exp the window sum uses.
+ * rounded (float)exp((double)x), 3 an FMA-pipe polynomial exp, 4 the MUFU
+ * exp (ex2.approx of x*log2e) the window sum uses by default.
  * Used by the GPU tests to bound the sum term's error and bias. */
 int quasar_selftest_exp(const float *d_x, float *d_out, int n, int which, void *stream);
 

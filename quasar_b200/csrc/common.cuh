@@ -156,17 +156,43 @@ __device__ __forceinline__ f32x2 exp_poly2(float a, float b) {
                  __int_as_float(__float_as_int(pb) + (__float_as_int(tb) << 23)));
 }
 
-// The exp used for the terms of the window sum (compile-time choice).
+// 2^t from the MUFU unit (PTX ex2.approx.ftz.f32: ~2 ulp; -inf gives +0).
+__device__ __forceinline__ float ex2_approx(float t) {
+    float e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(t));
+    return e;
+}
+
+// e^x = 2^(x * float(log2 e)) for x <= 0: one multiply and one MUFU op, no
+// clamp needed (x = -inf gives 0). Error: ex2.approx (~2 ulp) plus the
+// rounding of the product (|x*log2e| * 2^-24 absolute in the exponent); both
+// are small for the terms that carry the window sum (x near 0).
+__device__ __forceinline__ float exp_fast(float x) {
+    return ex2_approx(__fmul_rn(x, 1.44269502162933349609375f));
+}
+// Two lanes: one packed multiply, two MUFU ops.
+__device__ __forceinline__ f32x2 exp_fast2(f32x2 x) {
+    const f32x2 kLog2e = 0x3fb8aa3b3fb8aa3bull;
+    float t0, t1;
+    unpack2(mul2(x, kLog2e), t0, t1);
+    return pack2(ex2_approx(t0), ex2_approx(t1));
+}
+
+// The exp used for the terms of the window sum (compile-time choice):
+// 0 expf, 1 exp_term, 2 exp_poly, 3 exp_fast (MUFU), 4 half of the pairs of
+// a tile on MUFU and half on the FMA pipe (exp_poly), balancing the two units.
 #ifndef QS_SUM_EXP
-#define QS_SUM_EXP 2
+#define QS_SUM_EXP 3
 #endif
 __device__ __forceinline__ float sum_term_exp(float x) {
 #if QS_SUM_EXP == 0
     return expf(x);
 #elif QS_SUM_EXP == 1
     return exp_term(x);
-#else
+#elif QS_SUM_EXP == 2 || QS_SUM_EXP == 4
     return exp_poly(x);
+#else
+    return exp_fast(x);
 #endif
 }
 

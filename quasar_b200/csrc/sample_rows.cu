@@ -907,6 +907,43 @@ __device__ __forceinline__ void stream_tiles(const Row& R, Src& src, Shared& s, 
     }
 }
 
+// Penalized elements are left out of the stream (read as -inf); their
+// penalized values re-enter through claim_penalized.
+__device__ __forceinline__ void exclude_penalized(const Row& R, const uint8_t* bits8, float* v, int o0, int o1) {
+    const uint32_t m0 = o0 < R.noct ? bits8[o0] : 0u;
+    const uint32_t m1 = o1 < R.noct ? bits8[o1] : 0u;
+    if (m0 | m1) {
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            if (m0 & (1u << k)) v[k] = -INFINITY;
+            if (m1 & (1u << k)) v[8 + k] = -INFINITY;
+        }
+    }
+}
+
+// Hands every distinct in-range history id of the row to f(id, penalized
+// logit) (sample.c:118-128) exactly once: the thread whose atomic clears the
+// id's bit owns it. Leaves the bitset all zero. Callers synchronise first so
+// that no thread still reads the bitset.
+template <class F>
+__device__ __forceinline__ void claim_penalized(const RowCtx& c, const Row& R, uint32_t* bits, F&& f) {
+    for (int i = threadIdx.x; i < c.len; i += CONSUMERS) {
+        const int id = c.ring[(c.head + i) % c.cap];
+        if (id >= 0 && id < R.V) {
+            const uint32_t bit = 1u << (id & 31);
+            if (atomicAnd(&bits[id >> 5], ~bit) & bit) f(id, penalize(__ldg(R.ptr + id), R.rp));
+        }
+    }
+}
+
+// Sets the bits of the row's history ids again (after claim_penalized).
+__device__ __forceinline__ void set_bits(const RowCtx& c, const Row& R, uint32_t* bits) {
+    for (int i = threadIdx.x; i < c.len; i += CONSUMERS) {
+        const int id = c.ring[(c.head + i) % c.cap];
+        if (id >= 0 && id < R.V) atomicOr(&bits[id >> 5], 1u << (id & 31));
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Kernel A, one row: greedy rows are finished here; a stochastic row is
 // streamed once and leaves its summary in the workspace (max M, 1/sum, the
@@ -928,14 +965,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
             float v[16];
             src.get(R, it, v, s);
             const int o0 = it * OCT_TILE + tid, o1 = o0 + CONSUMERS;
-            if (R.use_pen) {
-                const uint32_t m0 = o0 < R.noct ? bits8[o0] : 0u;
-                const uint32_t m1 = o1 < R.noct ? bits8[o1] : 0u;
-                if (m0 | m1) {
-                    apply_pen_oct(v, m0, R.rp);
-                    apply_pen_oct(v + 8, m1, R.rp);
-                }
-            }
+            if (R.use_pen) exclude_penalized(R, bits8, v, o0, o1);
             src.release();
             float mt = v[0];
 #pragma unroll
@@ -946,6 +976,17 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
                 bv = mt;
                 bi = j < 8 ? 8 * o0 + j : 8 * o1 + (j - 8);
             }
+        }
+        if (R.use_pen) {
+            csync();
+            // penalized ids compete by (value desc, id asc); -inf never wins,
+            // so an all -inf row still gives id 0 (sample.c:130-134)
+            claim_penalized(c, R, bits, [&](int id, float l) {
+                if (l > bv || (l == bv && id < bi && l > -INFINITY)) {
+                    bv = l;
+                    bi = id;
+                }
+            });
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -986,15 +1027,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
     float m = -INFINITY;
     double S = 0.0;
     auto body = [&](float (&v)[16], int it) {
-        const int o0 = it * OCT_TILE + tid, o1 = o0 + CONSUMERS;
-        if (R.use_pen) {
-            const uint32_t m0 = o0 < R.noct ? bits8[o0] : 0u;
-            const uint32_t m1 = o1 < R.noct ? bits8[o1] : 0u;
-            if (m0 | m1) {
-                apply_pen_oct(v, m0, R.rp);
-                apply_pen_oct(v + 8, m1, R.rp);
-            }
-        }
+        if (R.use_pen) exclude_penalized(R, bits8, v, it * OCT_TILE + tid, it * OCT_TILE + tid + CONSUMERS);
         // sample.c:142: sc = l * inv_t, rounded exactly like the reference
         // (packed pairs: each lane is the same IEEE multiply)
         f32x2 sc2[8];
@@ -1017,10 +1050,16 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
             const f32x2 nm2 = pack2(-m, -m);
 #pragma unroll
             for (int j = 0; j < 8; j++) {
-#if QS_SUM_EXP == 2
-                float x0, x1;
-                unpack2(add2(sc2[j], nm2), x0, x1);
-                e[j] = exp_poly2(x0, x1);
+#if QS_SUM_EXP == 3
+                e[j] = exp_fast2(add2(sc2[j], nm2));
+#elif QS_SUM_EXP == 2 || QS_SUM_EXP == 4
+                if (QS_SUM_EXP == 4 && (j & 1) == 0) {
+                    e[j] = exp_fast2(add2(sc2[j], nm2));
+                } else {
+                    float x0, x1;
+                    unpack2(add2(sc2[j], nm2), x0, x1);
+                    e[j] = exp_poly2(x0, x1);
+                }
 #else
                 e[j] = pack2(sum_term_exp(__fsub_rn(sc[2 * j], m)), sum_term_exp(__fsub_rn(sc[2 * j + 1], m)));
 #endif
@@ -1044,13 +1083,24 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
         }
     };
     stream_tiles(R, src, s, body);
+    if (R.use_pen) {
+        csync();
+        // the penalized elements join the running max and sum exactly
+        claim_penalized(c, R, bits, [&](int, float l) {
+            const float sc = __fmul_rn(l, R.inv_t);
+            if (sc > m) {
+                S = (m > -INFINITY ? S * exp((double)m - (double)sc) : 0.0) + 1.0;
+                m = sc;
+            } else if (sc > -INFINITY) {
+                S += exp((double)sc - (double)m);
+            }
+        });
+    }
     a.work_tfmax[(int64_t)row * CONSUMERS + tid] = m;
     const float M = block_max_f(m, s);
     const double contrib = (m > -INFINITY) ? S * exp((double)m - (double)M) : 0.0;
     const double Stot = block_sum_d(contrib, s);
     if (tid == 0) a.work_info[row] = make_float2(M, __double2float_rn(1.0 / Stot));
-    clear_bits(a, c, R, bits);
-    csync();
 }
 
 // ---------------------------------------------------------------------------
@@ -1085,7 +1135,7 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
     uint64_t st_rng = a.rng[row];
     const double u = rng_unit(&st_rng);  // sample.c:173: one step per stochastic row
     int path = QUASAR_PATH_SELECT;
-    bool done = false;
+    bool done = false, cleared = false;
     const bool by_minp = P.min_p > 0.0f;
     const bool by_topk = P.top_k > 0 && P.top_k <= TOPK_MAX;
     if (!(a.flags & QUASAR_FLAG_EXACT_SELECT) && (by_minp || by_topk)) {
@@ -1134,10 +1184,9 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
                 if (ok) {
                     load_oct_keep(R.ptr, o0, R.V, R.vec, sc);
                     load_oct_keep(R.ptr, o1, R.V, R.vec, sc + 8);
-                    if (R.use_pen) {
-                        apply_pen_oct(sc, o0 < R.noct ? bits8[o0] : 0u, R.rp);
-                        apply_pen_oct(sc + 8, o1 < R.noct ? bits8[o1] : 0u, R.rp);
-                    }
+                    // the tile bounds leave penalized elements out; they
+                    // come from the history below
+                    if (R.use_pen) exclude_penalized(R, bits8, sc, o0, o1);
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
                         sc[j] = __fmul_rn(sc[j], R.inv_t);
@@ -1162,6 +1211,17 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
                     }
                 }
             }
+        }
+        if (R.use_pen) {
+            csync();  // the re-reads are done with the bitset
+            claim_penalized(c, R, bits, [&](int id, float l) {
+                const float sc = __fmul_rn(l, R.inv_t);
+                if (sc >= lo) {
+                    const int pos = atomicAdd(&s.ncand, 1);
+                    if (pos < room) buf[CAP - 1 - pos] = ((uint64_t)__float_as_uint(sc) << 32) | (uint32_t)id;
+                }
+            });
+            cleared = true;
         }
         csync();
         const int nk = nq_all <= QMAX ? s.ncand : CAP + 1;
@@ -1193,6 +1253,10 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
     }
     if (!done) {
         csync();
+        if (cleared) {
+            set_bits(c, R, bits);
+            csync();
+        }
         select_path(R, bits8, reinterpret_cast<Hist*>(buf), P, u, s);
     }
     row_finish(a, row, c, R, bits, path, st_rng, s);
