@@ -135,15 +135,19 @@ int quasar_sampler_pick_batch(const float *d_logits, int64_t ld, int B, int V,
                               void *d_workspace, size_t workspace_bytes,
                               int flags, void *stream);
 
-/* Device workspace one quasar_sampler_pick_batch call of B rows needs (the
- * list of rows handed to the exact-select kernel). Pass d_workspace = NULL to
- * use a workspace the library allocates per device and keeps; that one is
- * shared, so concurrent calls on one device must each pass their own. */
-size_t quasar_sampler_workspace_bytes(int B);
+/* Device workspace one quasar_sampler_pick_batch call of B rows with history
+ * capacity hist_cap needs: the per-row summaries the streaming kernel leaves
+ * for the finishing kernel (row max and 1/sum, per-thread maxima, tile-max
+ * table, penalized-id list; ~20 KB per row at hist_cap 256). Pass
+ * d_workspace = NULL to use a workspace the library allocates per device and
+ * keeps; that one is shared, so concurrent calls on one device must each
+ * pass their own. */
+size_t quasar_sampler_workspace_bytes(int B, int hist_cap);
 
 /* Kernel launches one quasar_sampler_pick_batch call makes (2: the streaming
- * kernel and the exact-select kernel, which exits at once when no row needs
- * it), plus one 4-byte memset of the workspace counter. A row whose id comes
+ * kernel, which also finishes greedy rows, and the finishing kernel of the
+ * stochastic rows: cuts, exact select where needed, draw), plus one 4-byte
+ * memset of the workspace abort word. A row whose id comes
  * back -1 hit the bounded-wait timeout of the bulk-copy ring (a device fault,
  * not a sampling result). */
 int quasar_sampler_pick_batch_launches(void);

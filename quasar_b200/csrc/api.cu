@@ -134,7 +134,9 @@ const char* quasar_status_string(int status) {
 
 int quasar_sampler_pick_batch_launches(void) { return 2; }
 
-size_t quasar_sampler_workspace_bytes(int B) { return B > 0 ? qs::rows_workspace_bytes(B) : 0; }
+size_t quasar_sampler_workspace_bytes(int B, int hist_cap) {
+    return B > 0 ? qs::rows_workspace_bytes(B, hist_cap) : 0;
+}
 
 int quasar_sampler_pick_batch(const float* d_logits, int64_t ld, int B, int V,
                               const quasar_sample_params* d_params,
@@ -172,9 +174,10 @@ int quasar_sampler_pick_batch(const float* d_logits, int64_t ld, int B, int V,
     a.tma = tma && !(flags & QUASAR_FLAG_NO_TMA);
     void* ws = d_workspace;
     if (ws) {
-        if (workspace_bytes < qs::rows_workspace_bytes(B) || (uintptr_t)ws % 256 != 0) return QUASAR_EINVAL;
+        if (workspace_bytes < qs::rows_workspace_bytes(B, hist_cap) || (uintptr_t)ws % 256 != 0)
+            return QUASAR_EINVAL;
     } else {
-        const int rc = managed_workspace(qs::rows_workspace_bytes(B), &ws);
+        const int rc = managed_workspace(qs::rows_workspace_bytes(B, hist_cap), &ws);
         if (rc != QUASAR_OK) return rc;
     }
     const cudaError_t err = qs::launch_sample_rows(a, ws, (cudaStream_t)stream);

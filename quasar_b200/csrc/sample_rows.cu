@@ -52,6 +52,13 @@ constexpr int NSTAGE = 3;                      // ring depth of the TMA kernel
 constexpr int CAP = 4096;                      // candidate entries per row
 constexpr int TMAX_TILES = 40;                 // tile-max slots per thread (groups of tiles beyond)
 constexpr int TMAX_BYTES = TMAX_TILES * CONSUMERS;  // one byte per slot
+// Byte tables are laid out [slot / 4][thread][slot % 4]: a thread's four
+// consecutive slots share one 32-bit word, so kernel B reads them with one
+// coalesced load per four slots.
+__host__ __device__ constexpr int tbl_off(int slot, int tid) { return ((slot >> 2) * 256 + tid) * 4 + (slot & 3); }
+static_assert(TMAX_TILES % 4 == 0 && CONSUMERS == 256, "byte-table layout");
+constexpr int NCK = 6;                         // running-max checkpoints per thread: slots 0,1,3,7,15,31
+constexpr int ANC_BYTES = (NCK + 3) / 4 * 4 * CONSUMERS;  // checkpoint table per row (tbl_off layout)
 constexpr int TOPK_MAX = CONSUMERS;            // largest top_k the candidate path takes
 constexpr int QMAX = 4096;                     // qualifying thread-tiles re-read per row
 constexpr int NB = 1024;                       // radix bins per level (10 bits)
@@ -60,7 +67,7 @@ constexpr long long WAIT_CYCLES = 1ll << 32;   // ~2 s: bound on any mbarrier wa
 #define QS_LDG_DEPTH 1
 #endif
 #ifndef QS_A_CTAS
-#define QS_A_CTAS 4
+#define QS_A_CTAS 3
 #endif
 constexpr int LDG_DEPTH = QS_LDG_DEPTH;        // tiles in flight per thread, row-load kernel
 
@@ -79,6 +86,7 @@ struct Shared {
     int abort;            // a bounded wait gave up
     int ncand;            // candidate keys appended
     int nq;               // qualifying thread-tiles listed
+    int npen;             // penalized ids listed (kernel A)
     float tfmax[CONSUMERS];  // each consumer thread's final running max (scaled)
     float rf[CWARPS];
     double rd[CWARPS];
@@ -700,7 +708,7 @@ __device__ __forceinline__ uint8_t tile_deficit(float m, float slotmax) {
     return !(d < 255.0f) ? (uint8_t)255 : (uint8_t)(int)d;   // NaN / +inf -> 255
 }
 // Upper bound of a slot's max from its entry and its thread's final max.
-__device__ __forceinline__ float tile_bound(float thread_max, uint8_t d) {
+__device__ __forceinline__ float tile_bound(float thread_max, uint32_t d) {
     return __fsub_ru(thread_max, 0.125f * (float)d);
 }
 
@@ -809,11 +817,10 @@ struct RowCtx {
     const int32_t* ring;
 };
 
-// Row parameters, history ring and (with_bits) the penalty bitset of `row`.
-__device__ __forceinline__ RowCtx row_setup(const RowsArgs& a, int row, Row& R, uint32_t* bits) {
-    const int tid = threadIdx.x;
+// Row parameters and history ring of `row` (no shared-memory work).
+__device__ __forceinline__ RowCtx row_ctx(const RowsArgs& a, int row, const quasar_sample_params& pr, Row& R) {
     RowCtx c;
-    c.P = clamp_params(a.d_params ? a.d_params[row] : a.h_params);
+    c.P = clamp_params(pr);
     c.cap = a.hist ? a.hist_cap : 0;
     c.len = 0;
     c.head = 0;
@@ -832,12 +839,19 @@ __device__ __forceinline__ RowCtx row_setup(const RowsArgs& a, int row, Row& R, 
     R.rp = c.P.rp;
     R.inv_t = c.P.T > 0.0f ? __fdiv_rn(1.0f, c.P.T) : 0.0f;  // sample.c:137
     R.M = R.thr = R.inv = 0.0f;
+    return c;
+}
+
+// row_ctx plus the penalty bitset of the row's history ids (consumer threads).
+__device__ __forceinline__ RowCtx row_setup(const RowsArgs& a, int row, Row& R, uint32_t* bits, Shared& s) {
+    const RowCtx c = row_ctx(a, row, a.d_params ? a.d_params[row] : a.h_params, R);
     if (R.use_pen) {
-        for (int i = tid; i < c.len; i += CONSUMERS) {
+        for (int i = threadIdx.x; i < c.len; i += CONSUMERS) {
             const int id = c.ring[(c.head + i) % c.cap];
             if (id >= 0 && id < a.V) atomicOr(&bits[id >> 5], 1u << (id & 31));
         }
     }
+    if (threadIdx.x == 0) s.npen = 0;
     csync();
     return c;
 }
@@ -851,34 +865,38 @@ __device__ __forceinline__ void clear_bits(const RowsArgs& a, const RowCtx& c, c
     }
 }
 
-// Clears the bitset and writes the row's id, report, PRNG state and ring.
+// The row's id, report, PRNG state and ring append (one thread).
+__device__ __forceinline__ void write_row(const RowsArgs& a, int row, const RowCtx& c, int chosen, int nkept,
+                                          float p, float inv, int path, uint64_t st_rng) {
+    if (c.P.T > 0.0f) a.rng[row] = st_rng;
+    a.out[row] = chosen;
+    if (a.diag) {
+        quasar_pick_diag d;
+        d.n_kept = nkept;
+        d.p_chosen = p;
+        d.inv_sum = inv;
+        d.path = path;
+        a.diag[row] = d;
+    }
+    if (a.record && c.cap > 0 && a.hist_len && a.hist_head && chosen >= 0) {
+        int32_t* wring = a.hist + (int64_t)row * c.cap;
+        if (c.len < c.cap) {  // sample.c:85-87
+            wring[(c.head + c.len) % c.cap] = chosen;
+            a.hist_len[row] = c.len + 1;
+        } else {              // sample.c:88-90
+            wring[c.head] = chosen;
+            a.hist_head[row] = (c.head + 1) % c.cap;
+        }
+    }
+}
+
+// Clears the bitset and writes the row's outputs from the result slots.
 __device__ __forceinline__ void row_finish(const RowsArgs& a, int row, const RowCtx& c, const Row& R,
                                            uint32_t* bits, int path, uint64_t st_rng, Shared& s) {
     const int chosen = *reinterpret_cast<volatile int*>(&s.abort) ? -1 : s.res_id;
     clear_bits(a, c, R, bits);
     csync();
-    if (threadIdx.x == 0) {
-        if (c.P.T > 0.0f) a.rng[row] = st_rng;
-        a.out[row] = chosen;
-        if (a.diag) {
-            quasar_pick_diag d;
-            d.n_kept = s.res_nc;
-            d.p_chosen = s.res_p;
-            d.inv_sum = R.inv;
-            d.path = path;
-            a.diag[row] = d;
-        }
-        if (a.record && c.cap > 0 && a.hist_len && a.hist_head && chosen >= 0) {
-            int32_t* wring = a.hist + (int64_t)row * c.cap;
-            if (c.len < c.cap) {  // sample.c:85-87
-                wring[(c.head + c.len) % c.cap] = chosen;
-                a.hist_len[row] = c.len + 1;
-            } else {              // sample.c:88-90
-                wring[c.head] = chosen;
-                a.hist_head[row] = (c.head + 1) % c.cap;
-            }
-        }
-    }
+    if (threadIdx.x == 0) write_row(a, row, c, chosen, s.res_nc, s.res_p, R.inv, path, st_rng);
     csync();
 }
 
@@ -946,14 +964,23 @@ __device__ __forceinline__ void set_bits(const RowCtx& c, const Row& R, uint32_t
 
 // ---------------------------------------------------------------------------
 // Kernel A, one row: greedy rows are finished here; a stochastic row is
-// streamed once and leaves its summary in the workspace (max M, 1/sum, the
-// per-thread maxima and the tile-max table) for kernel B.
+// streamed once and leaves its summary in the workspace for kernel B: max M,
+// 1/sum, the per-thread maxima, the tile-max table with its checkpoint
+// anchors, and the list of penalized ids with their scaled logits.
+//
+// Tile-max table: one byte per thread and slot (a slot is g consecutive
+// tiles, g = 1 up to 40 tiles), the slot max's deficit below the thread's
+// running max m_j at the slot's end. The running max at slots 0,1,3,7,15,31
+// (checkpoints, kept in anc_s) is stored as a deficit below the thread's
+// final max, so slot j's max is bounded by final - (anchor deficit of the
+// first checkpoint >= j + slot deficit)/8: tight for early slots too.
 template <class Src>
-__device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src, uint32_t* bits, Shared& s) {
+__device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src, uint32_t* bits, float* anc_s,
+                                           Shared& s) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint8_t* bits8 = reinterpret_cast<const uint8_t*>(bits);
     Row R;
-    const RowCtx c = row_setup(a, row, R, bits);
+    const RowCtx c = row_setup(a, row, R, bits, s);
     const RowParams& P = c.P;
     src.begin(R);
 
@@ -1073,11 +1100,14 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
             S += (double)(e0 + e1);
         }
         if (g == 1) {
-            tmax[it * CONSUMERS + tid] = tile_deficit(m, mt);
+            tmax[tbl_off(it, tid)] = tile_deficit(m, mt);
+            if (it < 32 && ((it + 1) & it) == 0) anc_s[__popc(it) * CONSUMERS + tid] = m;
         } else {
             slotmax = fmaxf(slotmax, mt);
             if (it % g == g - 1 || it == R.ntiles - 1) {
-                tmax[(it / g) * CONSUMERS + tid] = tile_deficit(m, slotmax);
+                const int sl = it / g;
+                tmax[tbl_off(sl, tid)] = tile_deficit(m, slotmax);
+                if (sl < 32 && ((sl + 1) & sl) == 0) anc_s[__popc(sl) * CONSUMERS + tid] = m;
                 slotmax = -INFINITY;
             }
         }
@@ -1085,9 +1115,12 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
     stream_tiles(R, src, s, body);
     if (R.use_pen) {
         csync();
-        // the penalized elements join the running max and sum exactly
-        claim_penalized(c, R, bits, [&](int, float l) {
+        // the penalized elements join the running max and sum exactly, and
+        // are listed for kernel B
+        int2* pen = a.work_pen + (int64_t)row * a.hist_cap;
+        claim_penalized(c, R, bits, [&](int id, float l) {
             const float sc = __fmul_rn(l, R.inv_t);
+            pen[atomicAdd(&s.npen, 1)] = make_int2(id, __float_as_int(sc));
             if (sc > m) {
                 S = (m > -INFINITY ? S * exp((double)m - (double)sc) : 0.0) + 1.0;
                 m = sc;
@@ -1097,10 +1130,17 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
         });
     }
     a.work_tfmax[(int64_t)row * CONSUMERS + tid] = m;
+    {
+        const int nsl = (R.ntiles + g - 1) / g;
+        uint8_t* anc = a.work_anc + (int64_t)row * ANC_BYTES;
+#pragma unroll
+        for (int k = 0; k < NCK; k++)
+            if ((1 << k) - 1 < nsl) anc[tbl_off(k, tid)] = tile_deficit(m, anc_s[k * CONSUMERS + tid]);
+    }
     const float M = block_max_f(m, s);
     const double contrib = (m > -INFINITY) ? S * exp((double)m - (double)M) : 0.0;
     const double Stot = block_sum_d(contrib, s);
-    if (tid == 0) a.work_info[row] = make_float2(M, __double2float_rn(1.0 / Stot));
+    if (tid == 0) a.work_info[row] = make_float4(M, __double2float_rn(1.0 / Stot), __int_as_float(s.npen), 0.0f);
 }
 
 // ---------------------------------------------------------------------------
@@ -1109,68 +1149,109 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
 // Candidate path. The kept prefix lies above a threshold known once M is:
 // min_p -> sc >= M + ln(min_p) - 0.01 (every p >= min_p * p_max clears it);
 // top_k -> the k-th largest per-thread max less a tie margin (k distinct
-// elements reach it). Only thread-tiles whose bound clears the threshold are
-// read again. Rows it cannot bound take the exact select path.
+// elements reach it). Only thread-slots whose bound clears the threshold are
+// read again; penalized ids come from kernel A's list. Rows it cannot bound
+// take the exact select path.
+
+// Checkpoint slot index whose anchor bounds slot sl: the first of
+// 0,1,3,7,15,31 at or after sl (NCK = none: the thread's final max).
+__host__ __device__ constexpr int ck_of(int sl) {
+    return sl == 0 ? 0 : sl == 1 ? 1 : sl <= 3 ? 2 : sl <= 7 ? 3 : sl <= 15 ? 4 : sl <= 31 ? 5 : NCK;
+}
+
 __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t* buf, uint32_t* bits,
                                            Shared& s) {
     const int tid = threadIdx.x, lane = tid & 31;
     const uint8_t* bits8 = reinterpret_cast<const uint8_t*>(bits);
-    {
-        const quasar_sample_params pr = a.d_params ? a.d_params[row] : a.h_params;
-        if (!(pr.temperature > 0.0f)) return;  // greedy: finished by kernel A
-    }
+    const quasar_sample_params pr = a.d_params ? a.d_params[row] : a.h_params;
+    if (!(pr.temperature > 0.0f)) return;  // greedy: finished by kernel A
+    // every global load of the row summary, issued together
     Row R;
-    const RowCtx c = row_setup(a, row, R, bits);
+    const RowCtx c = row_ctx(a, row, pr, R);
     const RowParams& P = c.P;
-    const float2 info = a.work_info[row];
+    const float4 info = a.work_info[row];
+    const float m = a.work_tfmax[(int64_t)row * CONSUMERS + tid];  // this thread's max in kernel A
+    const int g = (R.ntiles + TMAX_TILES - 1) / TMAX_TILES;
+    const int nsl = (R.ntiles + g - 1) / g;
+    const uint8_t* tmax = a.work_tmax + (int64_t)row * TMAX_BYTES;
+    const uint8_t* anc = a.work_anc + (int64_t)row * ANC_BYTES;
+    constexpr int DW = TMAX_TILES / 4, EW = (NCK + 3) / 4;
+    uint32_t dw[DW], ew[EW];  // four slots per word (tbl_off)
+#pragma unroll
+    for (int q = 0; q < DW; q++)
+        dw[q] = 4 * q < nsl ? reinterpret_cast<const uint32_t*>(tmax)[q * CONSUMERS + tid] : 0xFFFFFFFFu;
+#pragma unroll
+    for (int q = 0; q < EW; q++) ew[q] = reinterpret_cast<const uint32_t*>(anc)[q * CONSUMERS + tid];
+    const int2* pen = a.work_pen + (int64_t)row * a.hist_cap;
+    const int2 pen0 = tid < a.hist_cap ? pen[tid] : make_int2(0, 0);  // used only if tid < npen
+    uint64_t st_rng = a.rng[row];
+
     R.M = info.x;
     R.inv = info.y;
     R.thr = __fsub_rn(R.M, 30.0f);
-    const float m = a.work_tfmax[(int64_t)row * CONSUMERS + tid];  // this thread's max in kernel A
+    // (an aborted kernel A leaves stale summaries: keep every index in range)
+    const int npen = min(max(__float_as_int(info.z), 0), a.hist_cap);
+    R.use_pen = npen > 0;
     s.tfmax[tid] = m;
-    const uint8_t* tmax = a.work_tmax + (int64_t)row * TMAX_BYTES;
-    const int g = (R.ntiles + TMAX_TILES - 1) / TMAX_TILES;
+    if (tid == 0) s.ncand = 0;
+    // bitset of the penalized ids: re-reads leave them out, the select path
+    // penalizes them
+    for (int i = tid; i < npen; i += CONSUMERS) {
+        const int id = (i == tid ? pen0 : pen[i]).x;
+        if (id >= 0 && id < R.V) atomicOr(&bits[id >> 5], 1u << (id & 31));
+    }
     csync();
 
-    uint64_t st_rng = a.rng[row];
     const double u = rng_unit(&st_rng);  // sample.c:173: one step per stochastic row
     int path = QUASAR_PATH_SELECT;
-    bool done = false, cleared = false;
+    bool done = false;
     const bool by_minp = P.min_p > 0.0f;
     const bool by_topk = P.top_k > 0 && P.top_k <= TOPK_MAX;
     if (!(a.flags & QUASAR_FLAG_EXACT_SELECT) && (by_minp || by_topk)) {
-        const int nslot = ((R.ntiles + g - 1) / g) * CONSUMERS;
         float tau = -INFINITY;
         if (by_minp) tau = __fadd_rn(R.M, (float)(log((double)fminf(P.min_p, 1.0f)) - 0.01));
         if (by_topk) tau = fmaxf(tau, topk_floor(P.top_k, s));
         const float lo = fmaxf(tau, R.thr);
-        if (tid == 0) {
-            s.ncand = 0;
-            s.nq = 0;
+        // qualifying thread-slots -> a shared list (bottom of buf), so the
+        // re-reads spread over all threads; positions from a block scan
+        uint64_t qmask = 0ull;
+        int cnt = 0;
+#pragma unroll
+        for (int sl = 0; sl < TMAX_TILES; sl++) {
+            const int ck = ck_of(sl);
+            // anchors of checkpoints past the last slot were never written:
+            // the thread's final max is the anchor there
+            const uint32_t ek = (ck < NCK && (1 << ck) - 1 < nsl) ? (ew[ck >> 2] >> (8 * (ck & 3))) & 255u : 0u;
+            const uint32_t ds = (dw[sl >> 2] >> (8 * (sl & 3))) & 255u;
+            const bool q = sl < nsl && tile_bound(m, ek + ds) >= lo;
+            qmask |= (uint64_t)(q ? 1u : 0u) << sl;
+            cnt += q ? 1 : 0;
         }
+        const int incl = warp_incl_scan(cnt, lane);
+        if (lane == 31) s.ri[tid >> 5] = incl;
         csync();
-        // qualifying thread-tiles -> a shared list (bottom of buf), so the
-        // re-reads spread over all threads and issue in one round; raw
-        // survivors are appended from the top of buf downwards
+        int off = incl - cnt, nq_all = 0;
+#pragma unroll
+        for (int w = 0; w < CWARPS; w++) {
+            if (w < (tid >> 5)) off += s.ri[w];
+            nq_all += s.ri[w];
+        }
         uint32_t* qlist = reinterpret_cast<uint32_t*>(buf);
-        {
-            // this thread's table entries, all loads in flight at once
-            const int nsl = nslot / CONSUMERS;
-            uint32_t d[TMAX_TILES];
-#pragma unroll
-            for (int sl = 0; sl < TMAX_TILES; sl++) d[sl] = sl < nsl ? tmax[sl * CONSUMERS + tid] : 255u;
-#pragma unroll
-            for (int sl = 0; sl < TMAX_TILES; sl++) {
-                if (sl < nsl && tile_bound(m, (uint8_t)d[sl]) >= lo) {
-                    const int q = atomicAdd(&s.nq, 1);
-                    if (q < QMAX) qlist[q] = (uint32_t)(sl * CONSUMERS + tid);
-                }
-            }
-        }
-        csync();
-        const int nq_all = s.nq;
+        for (; qmask; qmask &= qmask - 1ull, off++)
+            if (off < QMAX) qlist[off] = (uint32_t)((__ffsll((long long)qmask) - 1) * CONSUMERS + tid);
         const int nq = min(nq_all, QMAX);
         const int room = CAP - (nq + 1) / 2;  // entries left above the list
+        // raw survivors are appended from the top of buf downwards: first the
+        // penalized ids that clear the threshold
+        for (int i = tid; i < npen; i += CONSUMERS) {
+            const int2 pe = i == tid ? pen0 : pen[i];
+            const float sc = __int_as_float(pe.y);
+            if (sc >= lo && pe.x >= 0 && pe.x < R.V) {
+                const int pos = atomicAdd(&s.ncand, 1);
+                if (pos < room) buf[CAP - 1 - pos] = ((uint64_t)__float_as_uint(sc) << 32) | (uint32_t)pe.x;
+            }
+        }
+        csync();  // the list is complete
         for (int base = 0; base < nq; base += CONSUMERS) {
             const int i = base + tid;
             const uint32_t entry = i < nq ? qlist[i] : 0u;
@@ -1184,8 +1265,8 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
                 if (ok) {
                     load_oct_keep(R.ptr, o0, R.V, R.vec, sc);
                     load_oct_keep(R.ptr, o1, R.V, R.vec, sc + 8);
-                    // the tile bounds leave penalized elements out; they
-                    // come from the history below
+                    // the tile bounds leave penalized elements out; they came
+                    // from the list above
                     if (R.use_pen) exclude_penalized(R, bits8, sc, o0, o1);
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
@@ -1195,11 +1276,11 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
                     }
                 }
                 // one shared atomic per warp reserves the slots
-                const int cnt = __popc(mask);
-                const int incl = warp_incl_scan(cnt, lane);
+                const int cnt2 = __popc(mask);
+                const int incl2 = warp_incl_scan(cnt2, lane);
                 int pos = 0;
-                if (lane == 31 && incl > 0) pos = atomicAdd(&s.ncand, incl);
-                pos = __shfl_sync(FULL, pos, 31) + incl - cnt;
+                if (lane == 31 && incl2 > 0) pos = atomicAdd(&s.ncand, incl2);
+                pos = __shfl_sync(FULL, pos, 31) + incl2 - cnt2;
                 if (mask) {
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
@@ -1211,17 +1292,6 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
                     }
                 }
             }
-        }
-        if (R.use_pen) {
-            csync();  // the re-reads are done with the bitset
-            claim_penalized(c, R, bits, [&](int id, float l) {
-                const float sc = __fmul_rn(l, R.inv_t);
-                if (sc >= lo) {
-                    const int pos = atomicAdd(&s.ncand, 1);
-                    if (pos < room) buf[CAP - 1 - pos] = ((uint64_t)__float_as_uint(sc) << 32) | (uint32_t)id;
-                }
-            });
-            cleared = true;
         }
         csync();
         const int nk = nq_all <= QMAX ? s.ncand : CAP + 1;
@@ -1237,9 +1307,9 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
                 uint64_t* area = buf + CAP - n2;  // n2 <= CAP: in place, padded below
                 for (int i = tid; i < n2 - nk; i += CONSUMERS) area[i] = 0ull;
                 for (int i = n2 - nk + tid; i < n2; i += CONSUMERS) {
-                    const uint64_t e = area[i];
-                    const float v = __uint_as_float((uint32_t)(e >> 32));
-                    area[i] = ((uint64_t)p_key(v, R.M, R.thr, R.inv) << 32) | (uint32_t)(~(uint32_t)e);
+                    const uint64_t en = area[i];
+                    const float v = __uint_as_float((uint32_t)(en >> 32));
+                    area[i] = ((uint64_t)p_key(v, R.M, R.thr, R.inv) << 32) | (uint32_t)(~(uint32_t)en);
                 }
                 csync();
                 bitonic_desc(area, n2);
@@ -1253,13 +1323,16 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
     }
     if (!done) {
         csync();
-        if (cleared) {
-            set_bits(c, R, bits);
-            csync();
-        }
         select_path(R, bits8, reinterpret_cast<Hist*>(buf), P, u, s);
     }
-    row_finish(a, row, c, R, bits, path, st_rng, s);
+    const int chosen = *reinterpret_cast<volatile int*>(&s.abort) ? -1 : s.res_id;
+    for (int i = tid; i < npen; i += CONSUMERS) {
+        const int id = (i == tid ? pen0 : pen[i]).x;
+        if (id >= 0 && id < R.V) bits[id >> 5] = 0u;
+    }
+    csync();
+    if (tid == 0) write_row(a, row, c, chosen, s.res_nc, s.res_p, R.inv, path, st_rng);
+    csync();
 }
 
 // ---------------------------------------------------------------------------
@@ -1271,11 +1344,12 @@ __global__ void __launch_bounds__(CONSUMERS, QS_A_CTAS) sample_rows_ldg(RowsArgs
     extern __shared__ __align__(128) unsigned char dyn[];
     uint32_t* bits = reinterpret_cast<uint32_t*>(dyn);
     __shared__ Shared s;
+    __shared__ float anc_s[NCK * CONSUMERS];
     for (int i = threadIdx.x; i < a.nwords; i += CONSUMERS) bits[i] = 0u;
     if (threadIdx.x == 0) s.abort = 0;
     csync();
     LdgSource src;
-    for (int row = blockIdx.x; row < a.B; row += gridDim.x) stream_row(a, row, src, bits, s);
+    for (int row = blockIdx.x; row < a.B; row += gridDim.x) stream_row(a, row, src, bits, anc_s, s);
 }
 
 __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a) {
@@ -1284,6 +1358,7 @@ __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a)
     uint32_t* bits = reinterpret_cast<uint32_t*>(dyn + NSTAGE * TILE_BYTES);
     uint64_t* bars = reinterpret_cast<uint64_t*>(dyn + NSTAGE * TILE_BYTES + ((a.nwords * 4 + 7) & ~7));
     __shared__ Shared s;
+    __shared__ float anc_s[NCK * CONSUMERS];
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + NSTAGE);
     if (threadIdx.x == 0) {
         for (int i = 0; i < NSTAGE; i++) {
@@ -1326,7 +1401,7 @@ __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a)
     src.full0 = full0;
     src.empty0 = empty0;
     src.g = 0;
-    for (int row = blockIdx.x; row < a.B; row += gridDim.x) stream_row(a, row, src, bits, s);
+    for (int row = blockIdx.x; row < a.B; row += gridDim.x) stream_row(a, row, src, bits, anc_s, s);
     // After an abort, give chunks still in flight a bounded chance to land
     // before the CTA (and its shared memory) goes away; the rows of this CTA
     // are marked failed (id -1) by kernel B through the abort word.
@@ -1367,9 +1442,12 @@ size_t rows_finish_smem_bytes(int V) {  // kernel B
     return (size_t)rows::FINISH_SCRATCH + (size_t)nwords_for(V) * sizeof(uint32_t);
 }
 
-// [abort word][pad][info B x float2][tfmax B x 256 floats][tmax B x TMAX_BYTES]
-size_t rows_workspace_bytes(int B) {
-    return (size_t)256 + (size_t)B * (8 + 4 * rows::CONSUMERS + rows::TMAX_BYTES);
+// [abort word][pad][info B x float4][tfmax B x 256 floats][penalized list B x
+// hist_cap x int2][tmax B x TMAX_BYTES][anchors B x ANC_BYTES]
+size_t rows_workspace_bytes(int B, int hist_cap) {
+    const size_t per_row = 16 + 4 * rows::CONSUMERS + 8 * (size_t)(hist_cap > 0 ? hist_cap : 0) +
+                           rows::TMAX_BYTES + rows::ANC_BYTES;
+    return (size_t)256 + (size_t)B * per_row;
 }
 
 int rows_threads() { return rows::CONSUMERS; }
@@ -1404,11 +1482,20 @@ cudaError_t configure(KernelCfg& cfg, const void* fn, int threads, size_t smem, 
 cudaError_t launch_sample_rows(const RowsArgs& args, void* workspace, cudaStream_t stream) {
     RowsArgs a = args;
     a.nwords = nwords_for(args.V);
-    char* ws = reinterpret_cast<char*>(workspace);
+    char* ws = reinterpret_cast<char*>(workspace);  // layout of rows_workspace_bytes
+    const size_t B = (size_t)args.B, H = (size_t)(args.hist && args.hist_cap > 0 ? args.hist_cap : 0);
+    a.hist_cap = (int)H;
     a.work_abort = reinterpret_cast<int*>(ws);
-    a.work_info = reinterpret_cast<float2*>(ws + 256);
-    a.work_tfmax = reinterpret_cast<float*>(ws + 256 + (size_t)args.B * 8);
-    a.work_tmax = reinterpret_cast<uint8_t*>(ws + 256 + (size_t)args.B * (8 + 4 * rows::CONSUMERS));
+    ws += 256;
+    a.work_info = reinterpret_cast<float4*>(ws);
+    ws += B * 16;
+    a.work_tfmax = reinterpret_cast<float*>(ws);
+    ws += B * 4 * rows::CONSUMERS;
+    a.work_pen = reinterpret_cast<int2*>(ws);
+    ws += B * 8 * H;
+    a.work_tmax = reinterpret_cast<uint8_t*>(ws);
+    ws += B * rows::TMAX_BYTES;
+    a.work_anc = reinterpret_cast<uint8_t*>(ws);
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
     if (err != cudaSuccess) return err;

@@ -29,15 +29,17 @@ struct RowsArgs {
     int nwords;  // bitset words (set by the launcher)
     // per-row summaries kernel A leaves for kernel B (workspace; set by the launcher)
     int* work_abort;
-    float2* work_info;      // (max scaled logit, 1/sum)
-    float* work_tfmax;      // [B][256] per-thread running maxima
+    float4* work_info;      // (max scaled logit, 1/sum, penalized count as int bits, 0)
+    float* work_tfmax;      // [B][256] per-thread final maxima
+    int2* work_pen;         // [B][hist_cap] (id, scaled penalized logit as int bits)
     uint8_t* work_tmax;     // [B][TMAX] tile-max deficits
+    uint8_t* work_anc;      // [B][NCK][256] checkpoint deficits below the thread's final max
 };
 
 size_t rows_smem_bytes(int V);      // one-CTA-per-row kernel
 size_t rows_tma_smem_bytes(int V);  // persistent bulk-copy ring kernel
 size_t rows_finish_smem_bytes(int V);
-size_t rows_workspace_bytes(int B);  // device workspace of one launch
+size_t rows_workspace_bytes(int B, int hist_cap);  // device workspace of one launch
 int rows_threads();
 // Launches kernel A (one streaming pass per row) and kernel B (cuts and draw).
 cudaError_t launch_sample_rows(const RowsArgs& args, void* workspace, cudaStream_t stream);

@@ -109,7 +109,7 @@ def pick_batch(logits, rng, *, params=None, d_params=None, hist=None, hist_len=N
     hist / hist_len / hist_head: int32 CUDA tensors [B, H] / [B] / [B].
     out: optional int32 [B] CUDA tensor; diag: optional int32 [B, 4] CUDA tensor
     (DIAG_DTYPE records). workspace: optional uint8 CUDA tensor of at least
-    ``workspace_bytes(B)`` bytes (default: the library's per-device one).
+    ``workspace_bytes(B, H)`` bytes (default: the library's per-device one).
     Returns ``out``. Launches on ``stream`` (a torch.cuda.Stream; default: the
     current stream).
     """
@@ -141,9 +141,9 @@ def pick_batch(logits, rng, *, params=None, d_params=None, hist=None, hist_len=N
     return out
 
 
-def workspace_bytes(B: int) -> int:
-    """Bytes of device workspace one pick_batch call over B rows needs."""
-    return int(lib().quasar_sampler_workspace_bytes(int(B)))
+def workspace_bytes(B: int, hist_cap: int = 0) -> int:
+    """Bytes of device workspace one pick_batch call over B rows with history capacity hist_cap needs."""
+    return int(lib().quasar_sampler_workspace_bytes(int(B), int(hist_cap)))
 
 
 def synth_logits(kind: int, seed: int, row0: int, B: int, V: int, scale: float, out, stream=None):

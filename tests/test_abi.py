@@ -83,7 +83,8 @@ def test_batch_rejects_missing_pointers():
     # an explicit workspace must be large enough and 256-byte aligned
     assert lib.quasar_sampler_pick_batch(P(16), 10, 1, 10, None, ctypes.byref(prm), P(16), None, 0,
                                          None, None, 0, P(16), None, P(256), 8, 0, None) == -1
-    assert lib.quasar_sampler_workspace_bytes(4096) >= 4096 * 12
+    assert lib.quasar_sampler_workspace_bytes(4096, 256) >= 4096 * (256 * 8 + 12)
+    assert lib.quasar_sampler_workspace_bytes(0, 256) == 0
 
 
 def test_pick_guards_without_gpu():
