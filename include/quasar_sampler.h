@@ -100,9 +100,9 @@ typedef struct {
 /* Flags for quasar_sampler_pick_batch. */
 #define QUASAR_FLAG_EXACT_SELECT  1  /* route every stochastic row through the
                                         radix-select path (same results; slower) */
-#define QUASAR_FLAG_NO_TMA        2  /* use the one-CTA-per-row register-load kernel
-                                        even where the bulk-copy ring applies
-                                        (same results) */
+#define QUASAR_FLAG_NO_TMA        2  /* stream with 256-bit register loads even
+                                        where the bulk-copy ring applies (same
+                                        results) */
 
 /* Sample B rows of d_logits (row r at d_logits + r*ld, V columns, fp32).
  *   d_params    [B] per-row parameters on the device, or NULL to use *h_params
@@ -119,8 +119,9 @@ typedef struct {
  *   d_diag      [B] optional report, or NULL.
  * Requirements: 1 <= V <= QUASAR_MAX_VOCAB, ld >= V. When the rows start
  * 16-byte aligned with ld % 4 == 0 and V % 4 == 0, persistent CTAs stream them
- * through a shared-memory ring filled by bulk copies (TMA); otherwise one CTA
- * per row reads them with 256-bit (32-byte aligned rows) or scalar loads. Finite logits
+ * through a shared-memory ring filled by bulk copies (TMA); otherwise the same
+ * persistent CTAs read them with 256-bit (32-byte aligned rows) or scalar
+ * loads. A second kernel finishes the stochastic rows. Finite logits
  * only (as in the reference, NaN/inf give unspecified picks). Asynchronous on
  * `stream`; returns after the launch. Replaces, batched, sample.h:29. */
 #define QUASAR_MAX_VOCAB (1 << 20)
