@@ -153,6 +153,34 @@ size_t quasar_sampler_workspace_bytes(int B, int hist_cap);
  * not a sampling result). */
 int quasar_sampler_pick_batch_launches(void);
 
+/* ---- batched sampler without allocation (no counterpart in the reference) -- */
+
+/* Size of the fixed device array that serves as the workspace of
+ * quasar_sampler_pick_batch_noalloc (about 2,180 rows at hist_cap 256). */
+#define QUASAR_NOALLOC_WORKSPACE_BYTES (32u << 20)
+
+/* quasar_sampler_pick_batch with the same arguments and results, but its
+ * workspace is a file-scope device array of QUASAR_NOALLOC_WORKSPACE_BYTES, so
+ * the call allocates nothing: for callers that have no device memory to spare
+ * at sampling time (engines that reserve free HBM for their KV cache) or must
+ * not take the synchronisation an allocation can bring. A call whose
+ * quasar_sampler_workspace_bytes(B, hist_cap) exceeds the array returns
+ * QUASAR_EOVERFLOW without touching the GPU. The array is shared by all calls
+ * on one device in the process: calls that overlap (two streams or threads)
+ * race on it and must be serialised by the caller. The first call on each
+ * device sets up (array address lookup, kernel attributes); make it before any
+ * stream capture. Every call clears the one word that must start at zero (the
+ * abort flag) with a memset on `stream`. */
+int quasar_sampler_pick_batch_noalloc(const float *d_logits, int64_t ld, int B, int V,
+                                      const quasar_sample_params *d_params,
+                                      const quasar_sample_params *h_params,
+                                      uint64_t *d_rng,
+                                      int32_t *d_hist, int hist_cap,
+                                      int32_t *d_hist_len, int32_t *d_hist_head,
+                                      int record,
+                                      int32_t *d_out, quasar_pick_diag *d_diag,
+                                      int flags, void *stream);
+
 /* ---- synthetic inputs (benchmark / test utility, not in the reference) ---- */
 
 #define QUASAR_SYNTH_NORMAL       0  /* Irwin-Hall N(0,1) * scale */

@@ -18,6 +18,7 @@ STATUS = {0: "ok", -1: "invalid argument", -2: "unsupported shape", -3: "CUDA er
 
 PATH_GREEDY, PATH_CANDIDATE, PATH_SELECT = 0, 1, 2
 FLAG_EXACT_SELECT = 1
+QUASAR_NOALLOC_WORKSPACE_BYTES = 32 << 20  # include/quasar_sampler.h
 SYNTH_NORMAL, SYNTH_GUMBEL_PEAK, SYNTH_ZIPF = 0, 1, 2
 
 # Every symbol include/quasar_sampler.h declares, with (argtypes, restype).
@@ -37,6 +38,8 @@ SIGNATURES = {
     "quasar_sampler_pick_batch": ([_P, _I64, _I, _I, _P, _P, _P, _P, _I, _P, _P, _I, _P, _P,
                                    _P, ctypes.c_size_t, _I, _P], _I),
     "quasar_sampler_pick_batch_launches": ([], _I),
+    "quasar_sampler_pick_batch_noalloc": ([_P, _I64, _I, _I, _P, _P, _P, _P, _I, _P, _P, _I, _P, _P,
+                                           _I, _P], _I),
     "quasar_sampler_workspace_bytes": ([_I, _I], ctypes.c_size_t),
     "quasar_synth_logits": ([_I, _U64, _I64, _I, _I, _I64, _F, _P, _P], _I),
     "quasar_synth_hist": ([_U64, _I64, _I, _I, _I, _P, _P], _I),
