@@ -98,6 +98,7 @@ struct Shared {
     float pf_lo, pf_hi;
     int res_id, res_nc, res_pos;
     float res_p;
+    float4 pen_lut[16];   // nibble n -> +0 / -inf per bit (penalized elements leave the stream)
     int cut_p, cut_m, cut_d;  // candidate cuts (atomicMin targets)
     double rsum;
 };
@@ -707,6 +708,11 @@ __device__ __forceinline__ uint8_t tile_deficit(float m, float slotmax) {
     const float d = __fmul_rd(__fsub_rd(m, slotmax), 8.0f);  // never above the true deficit
     return !(d < 255.0f) ? (uint8_t)255 : (uint8_t)(int)d;   // NaN / +inf -> 255
 }
+// tile_deficit as a 32-bit value, for packing four slots into one store
+// (fminf maps NaN to 255, like tile_deficit).
+__device__ __forceinline__ uint32_t deficit_byte(float m, float slotmax) {
+    return __float2uint_rd(fminf(__fmul_rd(__fsub_rd(m, slotmax), 8.0f), 255.0f));
+}
 // Upper bound of a slot's max from its entry and its thread's final max.
 __device__ __forceinline__ float tile_bound(float thread_max, uint32_t d) {
     return __fsub_ru(thread_max, 0.125f * (float)d);
@@ -925,6 +931,34 @@ __device__ __forceinline__ void stream_tiles(const Row& R, Src& src, Shared& s, 
     }
 }
 
+// Streaming form of exclude_penalized: the octets' bitset nibbles index a
+// 16-entry table of float4 {0 or -inf} that is added to the values (x + 0 =
+// x, x + -inf = -inf for finite x), with no per-element branch; warps with no
+// penalized element in the tile skip it.
+__device__ __forceinline__ void mask_penalized(const Row& R, const uint8_t* bits8, const float4* lut, float* v,
+                                               int o0, int o1) {
+    const uint32_t m0 = o0 < R.noct ? bits8[o0] : 0u;
+    const uint32_t m1 = o1 < R.noct ? bits8[o1] : 0u;
+    if (__any_sync(FULL, (m0 | m1) != 0u)) {
+        const float4 q[4] = {lut[m0 & 15u], lut[m0 >> 4], lut[m1 & 15u], lut[m1 >> 4]};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const f32x2 lo = add2(pack2(v[4 * k], v[4 * k + 1]), pack2(q[k].x, q[k].y));
+            const f32x2 hi = add2(pack2(v[4 * k + 2], v[4 * k + 3]), pack2(q[k].z, q[k].w));
+            unpack2(lo, v[4 * k], v[4 * k + 1]);
+            unpack2(hi, v[4 * k + 2], v[4 * k + 3]);
+        }
+    }
+}
+
+__device__ __forceinline__ void init_pen_lut(Shared& s) {
+    if (threadIdx.x < 16) {
+        const int n = threadIdx.x;
+        s.pen_lut[n] = make_float4((n & 1) ? -INFINITY : 0.0f, (n & 2) ? -INFINITY : 0.0f,
+                                   (n & 4) ? -INFINITY : 0.0f, (n & 8) ? -INFINITY : 0.0f);
+    }
+}
+
 // Penalized elements are left out of the stream (read as -inf); their
 // penalized values re-enter through claim_penalized.
 __device__ __forceinline__ void exclude_penalized(const Row& R, const uint8_t* bits8, float* v, int o0, int o1) {
@@ -992,7 +1026,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
             float v[16];
             src.get(R, it, v, s);
             const int o0 = it * OCT_TILE + tid, o1 = o0 + CONSUMERS;
-            if (R.use_pen) exclude_penalized(R, bits8, v, o0, o1);
+            if (R.use_pen) mask_penalized(R, bits8, s.pen_lut, v, o0, o1);
             src.release();
             float mt = v[0];
 #pragma unroll
@@ -1048,13 +1082,14 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
 
     // ---- one streaming pass: max, online window sum, tile maxima ----
     const int g = (R.ntiles + TMAX_TILES - 1) / TMAX_TILES;  // tiles per table slot
-    uint8_t* tmax = a.work_tmax + (int64_t)row * TMAX_BYTES;
+    uint32_t* tmax32 = reinterpret_cast<uint32_t*>(a.work_tmax + (int64_t)row * TMAX_BYTES);
+    uint32_t tword = 0u;  // four slot bytes of this thread, stored together (tbl_off layout)
     float slotmax = -INFINITY;
     const f32x2 inv_t2 = pack2(R.inv_t, R.inv_t);
     float m = -INFINITY;
     double S = 0.0;
     auto body = [&](float (&v)[16], int it) {
-        if (R.use_pen) exclude_penalized(R, bits8, v, it * OCT_TILE + tid, it * OCT_TILE + tid + CONSUMERS);
+        if (R.use_pen) mask_penalized(R, bits8, s.pen_lut, v, it * OCT_TILE + tid, it * OCT_TILE + tid + CONSUMERS);
         // sample.c:142: sc = l * inv_t, rounded exactly like the reference
         // (packed pairs: each lane is the same IEEE multiply)
         f32x2 sc2[8];
@@ -1100,13 +1135,21 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
             S += (double)(e0 + e1);
         }
         if (g == 1) {
-            tmax[tbl_off(it, tid)] = tile_deficit(m, mt);
+            tword |= deficit_byte(m, mt) << (8 * (it & 3));
+            if ((it & 3) == 3 || it == R.ntiles - 1) {
+                tmax32[(it >> 2) * CONSUMERS + tid] = tword;
+                tword = 0u;
+            }
             if (it < 32 && ((it + 1) & it) == 0) anc_s[__popc(it) * CONSUMERS + tid] = m;
         } else {
             slotmax = fmaxf(slotmax, mt);
             if (it % g == g - 1 || it == R.ntiles - 1) {
                 const int sl = it / g;
-                tmax[tbl_off(sl, tid)] = tile_deficit(m, slotmax);
+                tword |= deficit_byte(m, slotmax) << (8 * (sl & 3));
+                if ((sl & 3) == 3 || it == R.ntiles - 1) {
+                    tmax32[(sl >> 2) * CONSUMERS + tid] = tword;
+                    tword = 0u;
+                }
                 if (sl < 32 && ((sl + 1) & sl) == 0) anc_s[__popc(sl) * CONSUMERS + tid] = m;
                 slotmax = -INFINITY;
             }
@@ -1347,6 +1390,7 @@ __global__ void __launch_bounds__(CONSUMERS, QS_A_CTAS) sample_rows_ldg(RowsArgs
     __shared__ float anc_s[NCK * CONSUMERS];
     for (int i = threadIdx.x; i < a.nwords; i += CONSUMERS) bits[i] = 0u;
     if (threadIdx.x == 0) s.abort = 0;
+    init_pen_lut(s);
     csync();
     LdgSource src;
     for (int row = blockIdx.x; row < a.B; row += gridDim.x) stream_row(a, row, src, bits, anc_s, s);
@@ -1369,6 +1413,7 @@ __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a)
         s.abort = 0;
     }
     for (int i = threadIdx.x; i < a.nwords; i += blockDim.x) bits[i] = 0u;
+    init_pen_lut(s);
     __syncthreads();
 
     if (threadIdx.x >= CONSUMERS) {
