@@ -82,6 +82,15 @@ struct Hist {
 // kernel B scratch: candidate keys [CAP]; the select path's histograms alias it
 constexpr int FINISH_SCRATCH = (int)sizeof(Hist) > CAP * 8 ? (int)sizeof(Hist) : CAP * 8;
 
+// Counting sort of the candidate keys (kernel B): NBK buckets of the p key's
+// bits below the row's largest key, four per consumer thread.
+constexpr int NBK = 1024;
+constexpr int BK_MAX = 256;  // largest bucket the in-bucket ranking takes
+struct Buckets {
+    uint32_t cnt[NBK];
+    uint32_t start[NBK];
+};
+
 struct Shared {
     int abort;            // a bounded wait gave up
     int ncand;            // candidate keys appended
@@ -100,6 +109,7 @@ struct Shared {
     float res_p;
     float4 pen_lut[16];   // nibble n -> +0 / -inf per bit (penalized elements leave the stream)
     int cut_p, cut_m, cut_d;  // candidate cuts (atomicMin targets)
+    int big_bucket;           // a bucket of the counting sort exceeds BK_MAX
     double rsum;
 };
 
@@ -737,6 +747,88 @@ __device__ float topk_floor(int k, Shared& s) {
     return t - (1e-5f + 1e-5f * fabsf(t));
 }
 
+// Minimum of a non-negative int over the consumer threads.
+__device__ int block_min_i(int v, Shared& s) {
+    v = __reduce_min_sync(FULL, v);
+    if ((threadIdx.x & 31) == 0) s.ri[threadIdx.x >> 5] = v;
+    csync();
+    int r = s.ri[0];
+#pragma unroll
+    for (int i = 1; i < CWARPS; i++) r = min(r, s.ri[i]);
+    csync();
+    return r;
+}
+
+// Converts the nk raw (sc, id) entries at buf[CAP - nk, CAP) into (p, ~id)
+// keys and sorts them descending (requires nk <= CAP / 2): a counting sort
+// over NBK buckets of (largest key - key) >> sh, sh the smallest shift that
+// fits the row's key range (bucket order is key order; equal p share a
+// bucket), scattered to buf[0, nk); then every key finds its place inside its
+// bucket by counting the larger keys there, and lands at buf[CAP - nk + rank].
+// Returns the sorted keys, or nullptr when a bucket holds more than BK_MAX
+// keys (the converted keys are then left unsorted at buf[CAP - nk, CAP)).
+__device__ const uint64_t* bucket_sort_keys(uint64_t* buf, int nk, const Row& R, Buckets* bk, Shared& s) {
+    const int tid = threadIdx.x;
+    uint64_t* src = buf + CAP - nk;
+    int kmin = 0x7FFFFFFF;
+    for (int i = tid; i < nk; i += CONSUMERS) {
+        const uint64_t en = src[i];
+        const uint32_t pk = p_key(__uint_as_float((uint32_t)(en >> 32)), R.M, R.thr, R.inv);
+        src[i] = ((uint64_t)pk << 32) | (uint32_t)(~(uint32_t)en);
+        kmin = min(kmin, (int)pk);  // p keys are non-negative floats: < 2^31
+    }
+    for (int b = tid; b < NBK; b += CONSUMERS) bk->cnt[b] = 0u;
+    if (tid == 0) s.big_bucket = 0;
+    kmin = block_min_i(kmin, s);
+    // the largest p is that of the row max: (float)exp(0) * inv = inv
+    const uint32_t kmax = max(__float_as_uint(R.inv), (uint32_t)kmin);
+    int sh = 0;
+    while (((kmax - (uint32_t)kmin) >> sh) >= (uint32_t)NBK) sh++;
+    for (int i = tid; i < nk; i += CONSUMERS)
+        atomicAdd(&bk->cnt[(kmax - (uint32_t)(src[i] >> 32)) >> sh], 1u);
+    csync();
+    {
+        // exclusive scan of the counts: thread t owns buckets 4t .. 4t+3
+        constexpr int PER = NBK / CONSUMERS;
+        uint32_t c[PER], tot = 0u;
+#pragma unroll
+        for (int k = 0; k < PER; k++) {
+            c[k] = bk->cnt[PER * tid + k];
+            tot += c[k];
+            if (c[k] > (uint32_t)BK_MAX) s.big_bucket = 1;
+        }
+        const int lane = tid & 31, w = tid >> 5;
+        const uint32_t incl = warp_incl_scan(tot, lane);
+        if (lane == 31) s.ri[w] = (int)incl;
+        csync();
+        uint32_t start = incl - tot;
+        for (int k = 0; k < w; k++) start += (uint32_t)s.ri[k];
+#pragma unroll
+        for (int k = 0; k < PER; k++) {
+            bk->start[PER * tid + k] = start;  // the scatter's cursor
+            start += c[k];
+        }
+    }
+    csync();
+    if (s.big_bucket) return nullptr;
+    for (int i = tid; i < nk; i += CONSUMERS) {
+        const uint64_t key = src[i];
+        buf[atomicAdd(&bk->start[(kmax - (uint32_t)(key >> 32)) >> sh], 1u)] = key;
+    }
+    csync();
+    // bucket b now spans [start[b] - cnt[b], start[b]) of buf
+    for (int i = tid; i < nk; i += CONSUMERS) {
+        const uint64_t key = buf[i];
+        const int b = (int)((kmax - (uint32_t)(key >> 32)) >> sh);
+        const int e = (int)bk->start[b], b0 = e - (int)bk->cnt[b];
+        int rank = b0;
+        for (int q = b0; q < e; q++) rank += buf[q] > key ? 1 : 0;
+        src[rank] = key;
+    }
+    csync();
+    return src;
+}
+
 // ---------------------------------------------------------------------------
 // Tile sources: where the consumers' 16 elements per tile come from. The
 // element -> thread mapping is the same for both: octets it*OCT_TILE + tid and
@@ -1203,7 +1295,7 @@ __host__ __device__ constexpr int ck_of(int sl) {
 }
 
 __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t* buf, uint32_t* bits,
-                                           Shared& s) {
+                                           Buckets* bk, Shared& s) {
     const int tid = threadIdx.x, lane = tid & 31;
     const uint8_t* bits8 = reinterpret_cast<const uint8_t*>(bits);
     const quasar_sample_params pr = a.d_params ? a.d_params[row] : a.h_params;
@@ -1257,19 +1349,44 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
         const float lo = fmaxf(tau, R.thr);
         // qualifying thread-slots -> a shared list (bottom of buf), so the
         // re-reads spread over all threads; positions from a block scan
-        uint64_t qmask = 0ull;
-        int cnt = 0;
+        // A slot qualifies when thread max - (anchor + slot deficit)/8 >= lo,
+        // i.e. anchor + deficit <= X = floor(8 (max - lo)) (+1 of slack, so
+        // no qualifying slot is missed); four slots per byte-SIMD compare.
+        // Anchors of checkpoints past the last slot were never written: the
+        // thread's final max is the anchor there (deficit 0).
+        uint32_t keep0 = 0u, keep1 = 0u;
 #pragma unroll
-        for (int sl = 0; sl < TMAX_TILES; sl++) {
-            const int ck = ck_of(sl);
-            // anchors of checkpoints past the last slot were never written:
-            // the thread's final max is the anchor there
-            const uint32_t ek = (ck < NCK && (1 << ck) - 1 < nsl) ? (ew[ck >> 2] >> (8 * (ck & 3))) & 255u : 0u;
-            const uint32_t ds = (dw[sl >> 2] >> (8 * (sl & 3))) & 255u;
-            const bool q = sl < nsl && tile_bound(m, ek + ds) >= lo;
-            qmask |= (uint64_t)(q ? 1u : 0u) << sl;
-            cnt += q ? 1 : 0;
+        for (int k = 0; k < NCK; k++)
+            if ((1 << k) - 1 < nsl) (k < 4 ? keep0 : keep1) |= 255u << (8 * (k & 3));
+        const uint32_t ea = ew[0] & keep0, eb = ew[1] & keep1;
+        const float xd = __fmul_ru(__fsub_ru(m, lo), 8.0f);
+        const int X = !(xd < 1000.0f) ? 1000 : (xd < -1.0f ? -1 : (int)floorf(xd) + 1);  // NaN -> 1000
+        auto thr = [&](uint32_t ek) {  // slot bytes <= X - ek qualify; -1: none
+            const int tq = X - (int)ek;
+            return tq < 0 ? -1 : (tq > 255 ? 255 : tq);
+        };
+        uint64_t qmask = 0ull;
+#pragma unroll
+        for (int q = 0; q < DW; q++) {
+            const uint32_t d4 = dw[q];
+            uint32_t r;
+            if (q == 0) {  // slots 0, 1, 2-3: checkpoints 0, 1, 2
+                const int t0 = thr(ea & 255u), t1 = thr((ea >> 8) & 255u), t2 = thr((ea >> 16) & 255u);
+                r = (t0 >= 0 && (d4 & 255u) <= (uint32_t)t0 ? 1u : 0u) |
+                    (t1 >= 0 && ((d4 >> 8) & 255u) <= (uint32_t)t1 ? 2u : 0u) |
+                    (t2 >= 0 && ((d4 >> 16) & 255u) <= (uint32_t)t2 ? 4u : 0u) |
+                    (t2 >= 0 && (d4 >> 24) <= (uint32_t)t2 ? 8u : 0u);
+            } else {
+                // checkpoint of slots 4q..4q+3: 3 (q=1), 4 (q<=3), 5 (q<=7), none
+                const uint32_t ek = q == 1 ? (ea >> 24) : q <= 3 ? (eb & 255u) : q <= 7 ? ((eb >> 8) & 255u) : 0u;
+                const int tq = thr(ek);
+                const uint32_t cmp = __vcmpleu4(d4, (uint32_t)max(tq, 0) * 0x01010101u);  // 0xFF per slot <= tq
+                r = tq < 0 ? 0u : (((cmp >> 7) & 1u) | ((cmp >> 14) & 2u) | ((cmp >> 21) & 4u) | ((cmp >> 28) & 8u));
+            }
+            qmask |= (uint64_t)r << (4 * q);
         }
+        if (nsl < 64) qmask &= (1ull << nsl) - 1ull;
+        const int cnt = __popcll(qmask);
         const int incl = warp_incl_scan(cnt, lane);
         if (lane == 31) s.ri[tid >> 5] = incl;
         csync();
@@ -1295,42 +1412,60 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
             }
         }
         csync();  // the list is complete
-        for (int base = 0; base < nq; base += CONSUMERS) {
-            const int i = base + tid;
-            const uint32_t entry = i < nq ? qlist[i] : 0u;
-            const int sl = (int)(entry / CONSUMERS), owner = (int)(entry % CONSUMERS);
+        // two list entries per thread in flight per round
+        for (int base = 0; base < nq; base += 2 * CONSUMERS) {
             for (int t = 0; t < g; t++) {
-                const int it = sl * g + t;
-                const bool ok = i < nq && it < R.ntiles;
-                const int o0 = it * OCT_TILE + owner, o1 = o0 + CONSUMERS;
-                float sc[16];
-                uint32_t mask = 0u;
-                if (ok) {
-                    load_oct_keep(R.ptr, o0, R.V, R.vec, sc);
-                    load_oct_keep(R.ptr, o1, R.V, R.vec, sc + 8);
-                    // the tile bounds leave penalized elements out; they came
-                    // from the list above
-                    if (R.use_pen) exclude_penalized(R, bits8, sc, o0, o1);
+                float sc[2][16];
+                uint32_t mask[2] = {0u, 0u};
+                int o0[2], o1[2];
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        sc[j] = __fmul_rn(sc[j], R.inv_t);
-                        const int idx = j < 8 ? 8 * o0 + j : 8 * o1 + (j - 8);
-                        mask |= (sc[j] >= lo && idx < R.V ? 1u : 0u) << j;
+                for (int h = 0; h < 2; h++) {
+                    const int i = base + h * CONSUMERS + tid;
+                    const uint32_t entry = i < nq ? qlist[i] : 0u;
+                    const int sl = (int)(entry / CONSUMERS), owner = (int)(entry % CONSUMERS);
+                    const int it = sl * g + t;
+                    o0[h] = it * OCT_TILE + owner;
+                    o1[h] = o0[h] + CONSUMERS;
+                    if (i < nq && it < R.ntiles) {
+                        load_oct_keep(R.ptr, o0[h], R.V, R.vec, sc[h]);
+                        load_oct_keep(R.ptr, o1[h], R.V, R.vec, sc[h] + 8);
+                        mask[h] = 0xFFFFu;
                     }
                 }
+                int cnt2 = 0;
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    if (mask[h]) {
+                        // the tile bounds leave penalized elements out; they
+                        // came from the list above
+                        if (R.use_pen) exclude_penalized(R, bits8, sc[h], o0[h], o1[h]);
+                        uint32_t mk = 0u;
+#pragma unroll
+                        for (int j = 0; j < 16; j++) {
+                            sc[h][j] = __fmul_rn(sc[h][j], R.inv_t);
+                            const int idx = j < 8 ? 8 * o0[h] + j : 8 * o1[h] + (j - 8);
+                            mk |= (sc[h][j] >= lo && idx < R.V ? 1u : 0u) << j;
+                        }
+                        mask[h] = mk;
+                    }
+                    cnt2 += __popc(mask[h]);
+                }
                 // one shared atomic per warp reserves the slots
-                const int cnt2 = __popc(mask);
                 const int incl2 = warp_incl_scan(cnt2, lane);
                 int pos = 0;
                 if (lane == 31 && incl2 > 0) pos = atomicAdd(&s.ncand, incl2);
                 pos = __shfl_sync(FULL, pos, 31) + incl2 - cnt2;
-                if (mask) {
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        if (mask & (1u << j)) {
-                            const int idx = j < 8 ? 8 * o0 + j : 8 * o1 + (j - 8);
-                            if (pos < room) buf[CAP - 1 - pos] = ((uint64_t)__float_as_uint(sc[j]) << 32) | (uint32_t)idx;
-                            pos++;
+                for (int h = 0; h < 2; h++) {
+                    if (mask[h]) {
+#pragma unroll
+                        for (int j = 0; j < 16; j++) {
+                            if (mask[h] & (1u << j)) {
+                                const int idx = j < 8 ? 8 * o0[h] + j : 8 * o1[h] + (j - 8);
+                                if (pos < room)
+                                    buf[CAP - 1 - pos] = ((uint64_t)__float_as_uint(sc[h][j]) << 32) | (uint32_t)idx;
+                                pos++;
+                            }
                         }
                     }
                 }
@@ -1341,18 +1476,21 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
         if (nk > 0 && nk <= room) {
             const uint64_t* keys = buf;
             // raw entries live in buf[CAP - nk, CAP)
-            if (nk <= 256) keys_sorted<1>(buf, buf + CAP - nk, nk, R);
-            else if (nk <= 512) keys_sorted<2>(buf, buf + CAP - nk, nk, R);
-            else if (nk <= 1024) keys_sorted<4>(buf, buf + CAP - nk, nk, R);
-            else {
-                int n2 = 2048;
+            // counting sort; a full bitonic sort for very large or clustered lists
+            const uint64_t* sorted = nk <= CAP / 2 ? bucket_sort_keys(buf, nk, R, bk, s) : nullptr;
+            const bool converted = nk <= CAP / 2 && !sorted;
+            if (sorted) keys = sorted;
+            if (nk > CAP / 2 || converted) {
+                int n2 = 32;
                 while (n2 < nk) n2 <<= 1;
                 uint64_t* area = buf + CAP - n2;  // n2 <= CAP: in place, padded below
                 for (int i = tid; i < n2 - nk; i += CONSUMERS) area[i] = 0ull;
-                for (int i = n2 - nk + tid; i < n2; i += CONSUMERS) {
-                    const uint64_t en = area[i];
-                    const float v = __uint_as_float((uint32_t)(en >> 32));
-                    area[i] = ((uint64_t)p_key(v, R.M, R.thr, R.inv) << 32) | (uint32_t)(~(uint32_t)en);
+                if (!converted) {
+                    for (int i = n2 - nk + tid; i < n2; i += CONSUMERS) {
+                        const uint64_t en = area[i];
+                        const float v = __uint_as_float((uint32_t)(en >> 32));
+                        area[i] = ((uint64_t)p_key(v, R.M, R.thr, R.inv) << 32) | (uint32_t)(~(uint32_t)en);
+                    }
                 }
                 csync();
                 bitonic_desc(area, n2);
@@ -1381,7 +1519,7 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
 // ---------------------------------------------------------------------------
 // Kernels. Dynamic shared memory: kernel A row-load variant [bits]; kernel A
 // ring variant [ring NSTAGE x 16 KB][bits][full bars][empty bars]; kernel B
-// [scratch: candidate keys / select histograms][bits].
+// [scratch: candidate keys / select histograms][bits][counting-sort buckets].
 
 __global__ void __launch_bounds__(CONSUMERS, QS_A_CTAS) sample_rows_ldg(RowsArgs a) {
     extern __shared__ __align__(128) unsigned char dyn[];
@@ -1463,11 +1601,12 @@ __global__ void __launch_bounds__(CONSUMERS, 3) sample_rows_finish(RowsArgs a) {
     extern __shared__ __align__(128) unsigned char dyn[];
     uint64_t* buf = reinterpret_cast<uint64_t*>(dyn);
     uint32_t* bits = reinterpret_cast<uint32_t*>(dyn + FINISH_SCRATCH);
+    Buckets* bk = reinterpret_cast<Buckets*>(dyn + FINISH_SCRATCH + (((size_t)a.nwords * 4 + 15) & ~(size_t)15));
     __shared__ Shared s;
     for (int i = threadIdx.x; i < a.nwords; i += CONSUMERS) bits[i] = 0u;
     if (threadIdx.x == 0) s.abort = *reinterpret_cast<volatile int*>(a.work_abort);
     csync();
-    for (int row = blockIdx.x; row < a.B; row += gridDim.x) finish_row(a, row, buf, bits, s);
+    for (int row = blockIdx.x; row < a.B; row += gridDim.x) finish_row(a, row, buf, bits, bk, s);
 }
 
 }  // namespace rows
@@ -1483,8 +1622,8 @@ size_t rows_tma_smem_bytes(int V) {  // kernel A, ring variant
            2 * rows::NSTAGE * sizeof(uint64_t);
 }
 
-size_t rows_finish_smem_bytes(int V) {  // kernel B
-    return (size_t)rows::FINISH_SCRATCH + (size_t)nwords_for(V) * sizeof(uint32_t);
+size_t rows_finish_smem_bytes(int V) {  // kernel B: [scratch][bits][buckets]
+    return (size_t)rows::FINISH_SCRATCH + (((size_t)nwords_for(V) * 4 + 15) & ~(size_t)15) + sizeof(rows::Buckets);
 }
 
 // [abort word][pad][info B x float4][tfmax B x 256 floats][penalized list B x
