@@ -181,6 +181,62 @@ int quasar_sampler_pick_batch_noalloc(const float *d_logits, int64_t ld, int B, 
                                       int32_t *d_out, quasar_pick_diag *d_diag,
                                       int flags, void *stream);
 
+/* ---- vocab-sharded sampling (tensor-parallel LM heads; new, no counterpart
+ * in the reference) ----------------------------------------------------------
+ * Rank g of G holds global columns [col0, col0 + Vs) of every row; history
+ * ids stay global. A batch is sampled in three phases with two all-gathers
+ * between them (done by the caller, e.g. NCCL), and every rank ends with the
+ * same ids, PRNG states and rings as an unsharded quasar_sampler_pick_batch
+ * over the full rows (within the stochastic tolerance of the candidate path):
+ *   1. quasar_shard_stats      -> d_stats[B] per rank; all-gather -> [G][B]
+ *   2. quasar_shard_candidates -> d_cand[B][k] per rank; all-gather -> [G][B][k]
+ *   3. quasar_shard_finish     -> ids, PRNG steps, ring appends (every rank)
+ * Stochastic rows need 1 <= top_k <= k <= 256 (the merge is exact because
+ * the global top-k lies in the union of the shards' top-k); other stochastic
+ * rows, and rows whose candidates a shard cannot bound, come back as -1.
+ * Greedy rows merge the shards' penalized argmax (lowest global id on ties). */
+typedef struct {
+    float   max;   /* stochastic row: max scaled logit of the shard;
+                      greedy row: its largest penalized logit */
+    int32_t best;  /* greedy row: that logit's column in the shard (-1: none) */
+    double  sum;   /* stochastic row: sum of exp(sc - max) over the shard */
+} quasar_shard_stat;
+
+/* Phase 1. d_workspace (quasar_sampler_workspace_bytes(B, hist_cap) bytes)
+ * keeps per-row summaries for phase 2 of the same batch. */
+int quasar_shard_stats(const float *d_logits, int64_t ld, int B, int Vs, int64_t col0,
+                       const quasar_sample_params *d_params,
+                       const quasar_sample_params *h_params,
+                       const int32_t *d_hist, int hist_cap,
+                       const int32_t *d_hist_len, const int32_t *d_hist_head,
+                       quasar_shard_stat *d_stats,
+                       void *d_workspace, size_t workspace_bytes, int flags, void *stream);
+
+/* Phase 2, with every rank's stats gathered in rank order (d_all_stats
+ * [G][B]) and the workspace of phase 1: this rank's k best candidates per row
+ * by (p desc, global id asc), as keys (p bits << 32 | ~global id), 0-padded. */
+int quasar_shard_candidates(const float *d_logits, int64_t ld, int B, int Vs, int64_t col0,
+                            const quasar_sample_params *d_params,
+                            const quasar_sample_params *h_params,
+                            const int32_t *d_hist, int hist_cap,
+                            const int32_t *d_hist_len, const int32_t *d_hist_head,
+                            const quasar_shard_stat *d_all_stats, int G, int rank, int k,
+                            uint64_t *d_cand,
+                            void *d_workspace, size_t workspace_bytes, int flags, void *stream);
+
+/* Phase 3, with every rank's candidates gathered in rank order (d_all_cand
+ * [G][B][k]): merge, cuts and draw (sample.c:151-177), one PRNG step per
+ * stochastic row, optional ring append; d_out gets global ids. */
+int quasar_shard_finish(const uint64_t *d_all_cand, const quasar_shard_stat *d_all_stats,
+                        int G, int k, int B,
+                        const quasar_sample_params *d_params,
+                        const quasar_sample_params *h_params,
+                        uint64_t *d_rng,
+                        int32_t *d_hist, int hist_cap,
+                        int32_t *d_hist_len, int32_t *d_hist_head,
+                        int record,
+                        int32_t *d_out, quasar_pick_diag *d_diag, void *stream);
+
 /* ---- synthetic inputs (benchmark / test utility, not in the reference) ---- */
 
 #define QUASAR_SYNTH_NORMAL       0  /* Irwin-Hall N(0,1) * scale */

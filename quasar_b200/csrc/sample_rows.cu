@@ -110,6 +110,7 @@ struct Shared {
     float4 pen_lut[16];   // nibble n -> +0 / -inf per bit (penalized elements leave the stream)
     int cut_p, cut_m, cut_d;  // candidate cuts (atomicMin targets)
     int big_bucket;           // a bucket of the counting sort exceeds BK_MAX
+    uint32_t bk_hi[CWARPS];   // per-warp maxima of the counting sort's keys
     double rsum;
 };
 
@@ -208,11 +209,14 @@ __device__ __forceinline__ void apply_pen_oct(float* v, uint32_t m, float rp) {
 }
 
 // p key of one penalized, scaled logit: bits of p = (float)exp(sc - M) * inv,
-// 0 outside the window. Both paths use it, so they agree bit for bit.
+// 0 outside the window. Both paths use it, so they agree bit for bit. For
+// finite logits p <= 1; the clamp keeps every key that non-finite logits
+// could produce (inf, NaN, negative NaN bits) at or below the key of 1.0f,
+// so keys always index the histograms and buckets in range.
 __device__ __forceinline__ uint32_t p_key(float sc, float M, float thr, float inv) {
     if (!(sc >= thr)) return 0u;
     const float e = __double2float_rn(exp((double)__fsub_rn(sc, M)));
-    return __float_as_uint(__fmul_rn(e, inv));
+    return min(__float_as_uint(__fmul_rn(e, inv)), 0x3F800000u);
 }
 
 __device__ float block_max_f(float v, Shared& s) {
@@ -747,16 +751,23 @@ __device__ float topk_floor(int k, Shared& s) {
     return t - (1e-5f + 1e-5f * fabsf(t));
 }
 
-// Minimum of a non-negative int over the consumer threads.
-__device__ int block_min_i(int v, Shared& s) {
-    v = __reduce_min_sync(FULL, v);
-    if ((threadIdx.x & 31) == 0) s.ri[threadIdx.x >> 5] = v;
+// Minimum and maximum of an unsigned value over the consumer threads.
+__device__ void block_minmax_u(uint32_t& lo, uint32_t& hi, Shared& s) {
+    lo = __reduce_min_sync(FULL, lo);
+    hi = __reduce_max_sync(FULL, hi);
+    if ((threadIdx.x & 31) == 0) {
+        s.ri[threadIdx.x >> 5] = (int)lo;
+        s.bk_hi[threadIdx.x >> 5] = hi;
+    }
     csync();
-    int r = s.ri[0];
+    lo = (uint32_t)s.ri[0];
+    hi = s.bk_hi[0];
 #pragma unroll
-    for (int i = 1; i < CWARPS; i++) r = min(r, s.ri[i]);
+    for (int i = 1; i < CWARPS; i++) {
+        lo = min(lo, (uint32_t)s.ri[i]);
+        hi = max(hi, s.bk_hi[i]);
+    }
     csync();
-    return r;
 }
 
 // Converts the nk raw (sc, id) entries at buf[CAP - nk, CAP) into (p, ~id)
@@ -770,20 +781,20 @@ __device__ int block_min_i(int v, Shared& s) {
 __device__ const uint64_t* bucket_sort_keys(uint64_t* buf, int nk, const Row& R, Buckets* bk, Shared& s) {
     const int tid = threadIdx.x;
     uint64_t* src = buf + CAP - nk;
-    int kmin = 0x7FFFFFFF;
+    uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
     for (int i = tid; i < nk; i += CONSUMERS) {
         const uint64_t en = src[i];
         const uint32_t pk = p_key(__uint_as_float((uint32_t)(en >> 32)), R.M, R.thr, R.inv);
         src[i] = ((uint64_t)pk << 32) | (uint32_t)(~(uint32_t)en);
-        kmin = min(kmin, (int)pk);  // p keys are non-negative floats: < 2^31
+        kmin = min(kmin, pk);
+        kmax = max(kmax, pk);
     }
     for (int b = tid; b < NBK; b += CONSUMERS) bk->cnt[b] = 0u;
     if (tid == 0) s.big_bucket = 0;
-    kmin = block_min_i(kmin, s);
-    // the largest p is that of the row max: (float)exp(0) * inv = inv
-    const uint32_t kmax = max(__float_as_uint(R.inv), (uint32_t)kmin);
+    // every key lies in [kmin, kmax], so every bucket index is in [0, NBK)
+    block_minmax_u(kmin, kmax, s);
     int sh = 0;
-    while (((kmax - (uint32_t)kmin) >> sh) >= (uint32_t)NBK) sh++;
+    while (((kmax - kmin) >> sh) >= (uint32_t)NBK) sh++;
     for (int i = tid; i < nk; i += CONSUMERS)
         atomicAdd(&bk->cnt[(kmax - (uint32_t)(src[i] >> 32)) >> sh], 1u);
     csync();
@@ -913,7 +924,15 @@ struct RowCtx {
     RowParams P;
     int cap, len, head;
     const int32_t* ring;
+    int64_t col0;  // global id of column 0 (vocab shards; 0 otherwise)
 };
+
+// History entry i of the row as a column index of this matrix (negative or
+// >= V when the id is not one of its columns).
+__device__ __forceinline__ int ring_id(const RowCtx& c, int i) {
+    const int64_t id = (int64_t)c.ring[(c.head + i) % c.cap] - c.col0;
+    return (id >= 0 && id < 0x7FFFFFFF) ? (int)id : -1;
+}
 
 // Row parameters and history ring of `row` (no shared-memory work).
 __device__ __forceinline__ RowCtx row_ctx(const RowsArgs& a, int row, const quasar_sample_params& pr, Row& R) {
@@ -923,6 +942,7 @@ __device__ __forceinline__ RowCtx row_ctx(const RowsArgs& a, int row, const quas
     c.len = 0;
     c.head = 0;
     c.ring = nullptr;
+    c.col0 = a.col0;
     if (c.cap > 0) {
         c.ring = a.hist + (int64_t)row * c.cap;
         c.len = a.hist_len ? min(max(a.hist_len[row], 0), c.cap) : c.cap;
@@ -945,7 +965,7 @@ __device__ __forceinline__ RowCtx row_setup(const RowsArgs& a, int row, Row& R, 
     const RowCtx c = row_ctx(a, row, a.d_params ? a.d_params[row] : a.h_params, R);
     if (R.use_pen) {
         for (int i = threadIdx.x; i < c.len; i += CONSUMERS) {
-            const int id = c.ring[(c.head + i) % c.cap];
+            const int id = ring_id(c, i);
             if (id >= 0 && id < a.V) atomicOr(&bits[id >> 5], 1u << (id & 31));
         }
     }
@@ -957,7 +977,7 @@ __device__ __forceinline__ RowCtx row_setup(const RowsArgs& a, int row, Row& R, 
 __device__ __forceinline__ void clear_bits(const RowsArgs& a, const RowCtx& c, const Row& R, uint32_t* bits) {
     if (R.use_pen) {
         for (int i = threadIdx.x; i < c.len; i += CONSUMERS) {
-            const int id = c.ring[(c.head + i) % c.cap];
+            const int id = ring_id(c, i);
             if (id >= 0 && id < a.V) bits[id >> 5] = 0u;
         }
     }
@@ -1072,7 +1092,7 @@ __device__ __forceinline__ void exclude_penalized(const Row& R, const uint8_t* b
 template <class F>
 __device__ __forceinline__ void claim_penalized(const RowCtx& c, const Row& R, uint32_t* bits, F&& f) {
     for (int i = threadIdx.x; i < c.len; i += CONSUMERS) {
-        const int id = c.ring[(c.head + i) % c.cap];
+        const int id = ring_id(c, i);
         if (id >= 0 && id < R.V) {
             const uint32_t bit = 1u << (id & 31);
             if (atomicAnd(&bits[id >> 5], ~bit) & bit) f(id, penalize(__ldg(R.ptr + id), R.rp));
@@ -1083,7 +1103,7 @@ __device__ __forceinline__ void claim_penalized(const RowCtx& c, const Row& R, u
 // Sets the bits of the row's history ids again (after claim_penalized).
 __device__ __forceinline__ void set_bits(const RowCtx& c, const Row& R, uint32_t* bits) {
     for (int i = threadIdx.x; i < c.len; i += CONSUMERS) {
-        const int id = c.ring[(c.head + i) % c.cap];
+        const int id = ring_id(c, i);
         if (id >= 0 && id < R.V) atomicOr(&bits[id >> 5], 1u << (id & 31));
     }
 }
@@ -1166,8 +1186,18 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
             s.res_id = (besti == 0x7FFFFFFF || besti >= a.V) ? 0 : besti;
             s.res_nc = 0;
             s.res_p = 1.0f;
+            // a vocab shard: its best (value, column) joins the merge; -1 when
+            // every value is -inf (the merge then falls back to id 0)
+            if (a.shard_stats)
+                a.shard_stats[row] = quasar_shard_stat{best, (besti == 0x7FFFFFFF || besti >= a.V) ? -1 : besti,
+                                                       0.0};
         }
         csync();
+        if (a.shard_stats) {
+            clear_bits(a, c, R, bits);
+            csync();
+            return;
+        }
         row_finish(a, row, c, R, bits, QUASAR_PATH_GREEDY, 0, s);
         return;
     }
@@ -1275,7 +1305,10 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
     const float M = block_max_f(m, s);
     const double contrib = (m > -INFINITY) ? S * exp((double)m - (double)M) : 0.0;
     const double Stot = block_sum_d(contrib, s);
-    if (tid == 0) a.work_info[row] = make_float4(M, __double2float_rn(1.0 / Stot), __int_as_float(s.npen), 0.0f);
+    if (tid == 0) {
+        a.work_info[row] = make_float4(M, __double2float_rn(1.0 / Stot), __int_as_float(s.npen), 0.0f);
+        if (a.shard_stats) a.shard_stats[row] = quasar_shard_stat{M, -1, Stot};
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -1294,12 +1327,38 @@ __host__ __device__ constexpr int ck_of(int sl) {
     return sl == 0 ? 0 : sl == 1 ? 1 : sl <= 3 ? 2 : sl <= 7 ? 3 : sl <= 15 ? 4 : sl <= 31 ? 5 : NCK;
 }
 
+// Global max M and inv = (float)(1/sum) of a row split into vocab shards,
+// from the shards' (max, sum against that max) pairs - the same combination
+// as the one over threads inside a shard.
+__device__ __forceinline__ void shard_norm(const RowsArgs& a, int row, float& M, float& inv) {
+    float mx = -INFINITY;
+    for (int g = 0; g < a.shard_G; g++) mx = fmaxf(mx, a.all_stats[(int64_t)g * a.B + row].max);
+    double S = 0.0;
+    for (int g = 0; g < a.shard_G; g++) {
+        const quasar_shard_stat st = a.all_stats[(int64_t)g * a.B + row];
+        if (st.max > -INFINITY) S += st.sum * exp((double)st.max - (double)mx);
+    }
+    M = mx;
+    inv = __double2float_rn(1.0 / S);
+}
+
 __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t* buf, uint32_t* bits,
                                            Buckets* bk, Shared& s) {
     const int tid = threadIdx.x, lane = tid & 31;
     const uint8_t* bits8 = reinterpret_cast<const uint8_t*>(bits);
     const quasar_sample_params pr = a.d_params ? a.d_params[row] : a.h_params;
-    if (!(pr.temperature > 0.0f)) return;  // greedy: finished by kernel A
+    const bool shard = a.shard_cand != nullptr;  // a vocab shard: emit candidates, no draw
+    uint64_t* cand = shard ? a.shard_cand + (int64_t)row * a.shard_k : nullptr;
+    if (!(pr.temperature > 0.0f)) {
+        // greedy: finished by kernel A; a shard contributes its best column
+        if (shard && tid == 0) {
+            const quasar_shard_stat st = a.all_stats[(int64_t)a.shard_rank * a.B + row];
+            cand[0] = st.best >= 0 ? ((uint64_t)ord_key(st.max) << 32) | (uint32_t)(~(uint32_t)(a.col0 + st.best))
+                                   : 0ull;
+            for (int i = 1; i < a.shard_k; i++) cand[i] = 0ull;
+        }
+        return;
+    }
     // every global load of the row summary, issued together
     Row R;
     const RowCtx c = row_ctx(a, row, pr, R);
@@ -1319,10 +1378,11 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
     for (int q = 0; q < EW; q++) ew[q] = reinterpret_cast<const uint32_t*>(anc)[q * CONSUMERS + tid];
     const int2* pen = a.work_pen + (int64_t)row * a.hist_cap;
     const int2 pen0 = tid < a.hist_cap ? pen[tid] : make_int2(0, 0);  // used only if tid < npen
-    uint64_t st_rng = a.rng[row];
+    uint64_t st_rng = a.rng ? a.rng[row] : 0ull;
 
     R.M = info.x;
     R.inv = info.y;
+    if (shard) shard_norm(a, row, R.M, R.inv);  // the row's global max and 1/sum
     R.thr = __fsub_rn(R.M, 30.0f);
     // (an aborted kernel A leaves stale summaries: keep every index in range)
     const int npen = min(max(__float_as_int(info.z), 0), a.hist_cap);
@@ -1342,7 +1402,8 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
     bool done = false;
     const bool by_minp = P.min_p > 0.0f;
     const bool by_topk = P.top_k > 0 && P.top_k <= TOPK_MAX;
-    if (!(a.flags & QUASAR_FLAG_EXACT_SELECT) && (by_minp || by_topk)) {
+    // (a shard emits k candidates per row: its rows need 1 <= top_k <= k)
+    if (!(a.flags & QUASAR_FLAG_EXACT_SELECT) && (by_minp || by_topk) && (!shard || (by_topk && P.top_k <= a.shard_k))) {
         float tau = -INFINITY;
         if (by_minp) tau = __fadd_rn(R.M, (float)(log((double)fminf(P.min_p, 1.0f)) - 0.01));
         if (by_topk) tau = fmaxf(tau, topk_floor(P.top_k, s));
@@ -1496,11 +1557,35 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
                 bitonic_desc(area, n2);
                 keys = area;
             }
-            candidate_cuts(keys, nk, P, by_minp ? __fmul_rn(P.min_p, R.inv) : 0.0f, u, s);
+            if (shard) {
+                // the shard's first k keys in (p desc, id asc) order, ids made global
+                for (int i = tid; i < a.shard_k; i += CONSUMERS) {
+                    uint64_t key = 0ull;
+                    if (i < nk) {
+                        const uint64_t k0 = keys[i];
+                        key = (k0 & 0xFFFFFFFF00000000ull) | (uint32_t)(~(uint32_t)(a.col0 + (int64_t)(~(uint32_t)k0)));
+                    }
+                    cand[i] = key;
+                }
+            } else {
+                candidate_cuts(keys, nk, P, by_minp ? __fmul_rn(P.min_p, R.inv) : 0.0f, u, s);
+            }
             done = true;
             path = QUASAR_PATH_CANDIDATE;
         }
         csync();
+    }
+    if (shard) {
+        // a shard row the candidate path could not bound: no candidates (the
+        // merge reports id -1 for it)
+        if (!done)
+            for (int i = tid; i < a.shard_k; i += CONSUMERS) cand[i] = 0ull;
+        for (int i = tid; i < npen; i += CONSUMERS) {
+            const int id = (i == tid ? pen0 : pen[i]).x;
+            if (id >= 0 && id < R.V) bits[id >> 5] = 0u;
+        }
+        csync();
+        return;
     }
     if (!done) {
         csync();
@@ -1609,6 +1694,54 @@ __global__ void __launch_bounds__(CONSUMERS, 3) sample_rows_finish(RowsArgs a) {
     for (int row = blockIdx.x; row < a.B; row += gridDim.x) finish_row(a, row, buf, bits, bk, s);
 }
 
+// Merge of the vocab shards' candidates, one CTA per row: the G*k gathered
+// keys ([G][B][k]) sorted descending, then greedy rows take the first (the
+// largest penalized logit, lowest global id on ties) and stochastic rows the
+// cuts and draw of the candidate path over the merged list, with the row's
+// PRNG step and ring append. Every rank computes the same ids.
+__global__ void __launch_bounds__(CONSUMERS, 3) sample_rows_merge(RowsArgs a) {
+    extern __shared__ __align__(128) unsigned char dyn[];
+    uint64_t* buf = reinterpret_cast<uint64_t*>(dyn);
+    __shared__ Shared s;
+    const int tid = threadIdx.x;
+    const int n = a.shard_G * a.shard_k;
+    int n2 = 32;
+    while (n2 < n) n2 <<= 1;
+    for (int row = blockIdx.x; row < a.B; row += gridDim.x) {
+        const quasar_sample_params pr = a.d_params ? a.d_params[row] : a.h_params;
+        Row R;
+        const RowCtx c = row_ctx(a, row, pr, R);
+        for (int i = tid; i < n2; i += CONSUMERS) {
+            const int g = i / a.shard_k, j = i - g * a.shard_k;
+            buf[i] = i < n ? a.shard_cand[((int64_t)g * a.B + row) * a.shard_k + j] : 0ull;
+        }
+        csync();
+        bitonic_desc(buf, n2);
+        int cnt = 0;
+        for (int i = tid; i < n; i += CONSUMERS) cnt += (buf[i] >> 32) != 0ull ? 1 : 0;
+        const int nk = block_sum_i(cnt, s);  // real keys sort first
+        if (!(pr.temperature > 0.0f)) {
+            if (tid == 0)
+                write_row(a, row, c, nk > 0 ? (int)(~(uint32_t)buf[0]) : 0, 0, 1.0f, 0.0f, QUASAR_PATH_GREEDY, 0ull);
+        } else {
+            float M, inv;
+            shard_norm(a, row, M, inv);
+            uint64_t st_rng = a.rng[row];
+            const double u = rng_unit(&st_rng);  // sample.c:173
+            if (nk > 0) {
+                candidate_cuts(buf, nk, c.P, c.P.min_p > 0.0f ? __fmul_rn(c.P.min_p, inv) : 0.0f, u, s);
+            } else if (tid == 0) {
+                s.res_id = -1;  // a shard could not bound its candidates
+                s.res_nc = 0;
+                s.res_p = 0.0f;
+            }
+            csync();
+            if (tid == 0) write_row(a, row, c, s.res_id, s.res_nc, s.res_p, inv, QUASAR_PATH_CANDIDATE, st_rng);
+        }
+        csync();
+    }
+}
+
 }  // namespace rows
 
 static int nwords_for(int V) { return ((V + 31) >> 5) + 1; }
@@ -1641,7 +1774,7 @@ struct KernelCfg {
     size_t smem_set[64];
     int grid[64];  // resident CTAs of the kernel on each device
 };
-thread_local KernelCfg g_ldg = {}, g_tma = {}, g_fin = {};
+thread_local KernelCfg g_ldg = {}, g_tma = {}, g_fin = {}, g_merge = {};
 
 cudaError_t configure(KernelCfg& cfg, const void* fn, int threads, size_t smem, int dev) {
     cudaError_t err = cudaSuccess;
@@ -1663,11 +1796,12 @@ cudaError_t configure(KernelCfg& cfg, const void* fn, int threads, size_t smem, 
 }
 }  // namespace
 
-cudaError_t launch_sample_rows(const RowsArgs& args, void* workspace, cudaStream_t stream) {
-    RowsArgs a = args;
-    a.nwords = nwords_for(args.V);
-    char* ws = reinterpret_cast<char*>(workspace);  // layout of rows_workspace_bytes
-    const size_t B = (size_t)args.B, H = (size_t)(args.hist && args.hist_cap > 0 ? args.hist_cap : 0);
+namespace {
+// Points the workspace fields of a at the layout of rows_workspace_bytes.
+void layout_workspace(RowsArgs& a, void* workspace) {
+    a.nwords = nwords_for(a.V);
+    char* ws = reinterpret_cast<char*>(workspace);
+    const size_t B = (size_t)a.B, H = (size_t)(a.hist && a.hist_cap > 0 ? a.hist_cap : 0);
     a.hist_cap = (int)H;
     a.work_abort = reinterpret_cast<int*>(ws);
     ws += 256;
@@ -1680,11 +1814,17 @@ cudaError_t launch_sample_rows(const RowsArgs& args, void* workspace, cudaStream
     a.work_tmax = reinterpret_cast<uint8_t*>(ws);
     ws += B * rows::TMAX_BYTES;
     a.work_anc = reinterpret_cast<uint8_t*>(ws);
-    int dev = 0;
+}
+
+cudaError_t current_device(int& dev) {
     cudaError_t err = cudaGetDevice(&dev);
     if (err != cudaSuccess) return err;
-    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    err = cudaMemsetAsync(a.work_abort, 0, sizeof(int), stream);
+    return (dev < 0 || dev >= 64) ? cudaErrorInvalidDevice : cudaSuccess;
+}
+
+// Kernel A: clears the abort word, then streams every row once.
+cudaError_t launch_stream(const RowsArgs& a, int dev, cudaStream_t stream) {
+    cudaError_t err = cudaMemsetAsync(a.work_abort, 0, sizeof(int), stream);
     if (err != cudaSuccess) return err;
     if (a.tma) {
         const size_t smem = rows_tma_smem_bytes(a.V);
@@ -1697,12 +1837,62 @@ cudaError_t launch_sample_rows(const RowsArgs& args, void* workspace, cudaStream
         if (err != cudaSuccess) return err;
         rows::sample_rows_ldg<<<min(a.B, g_ldg.grid[dev]), rows::CONSUMERS, smem, stream>>>(a);
     }
-    err = cudaGetLastError();
-    if (err != cudaSuccess) return err;
+    return cudaGetLastError();
+}
+
+// Kernel B: one CTA per row.
+cudaError_t launch_finish(const RowsArgs& a, int dev, cudaStream_t stream) {
     const size_t fsmem = rows_finish_smem_bytes(a.V);
-    err = configure(g_fin, (const void*)rows::sample_rows_finish, rows::CONSUMERS, fsmem, dev);
+    cudaError_t err = configure(g_fin, (const void*)rows::sample_rows_finish, rows::CONSUMERS, fsmem, dev);
     if (err != cudaSuccess) return err;
     rows::sample_rows_finish<<<a.B, rows::CONSUMERS, fsmem, stream>>>(a);
+    return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_sample_rows(const RowsArgs& args, void* workspace, cudaStream_t stream) {
+    RowsArgs a = args;
+    layout_workspace(a, workspace);
+    int dev = 0;
+    cudaError_t err = current_device(dev);
+    if (err != cudaSuccess) return err;
+    err = launch_stream(a, dev, stream);
+    if (err != cudaSuccess) return err;
+    return launch_finish(a, dev, stream);
+}
+
+cudaError_t launch_shard_stats(const RowsArgs& args, void* workspace, cudaStream_t stream) {
+    RowsArgs a = args;
+    layout_workspace(a, workspace);
+    int dev = 0;
+    cudaError_t err = current_device(dev);
+    if (err != cudaSuccess) return err;
+    return launch_stream(a, dev, stream);
+}
+
+cudaError_t launch_shard_candidates(const RowsArgs& args, void* workspace, cudaStream_t stream) {
+    RowsArgs a = args;
+    layout_workspace(a, workspace);
+    int dev = 0;
+    cudaError_t err = current_device(dev);
+    if (err != cudaSuccess) return err;
+    return launch_finish(a, dev, stream);
+}
+
+size_t rows_merge_smem_bytes(int G, int k) {
+    size_t n2 = 32;
+    while (n2 < (size_t)G * (size_t)k) n2 <<= 1;
+    return n2 * sizeof(uint64_t);
+}
+
+cudaError_t launch_shard_merge(const RowsArgs& args, cudaStream_t stream) {
+    int dev = 0;
+    cudaError_t err = current_device(dev);
+    if (err != cudaSuccess) return err;
+    const size_t smem = rows_merge_smem_bytes(args.shard_G, args.shard_k);
+    err = configure(g_merge, (const void*)rows::sample_rows_merge, rows::CONSUMERS, smem, dev);
+    if (err != cudaSuccess) return err;
+    rows::sample_rows_merge<<<min(args.B, g_merge.grid[dev]), rows::CONSUMERS, smem, stream>>>(args);
     return cudaGetLastError();
 }
 

@@ -34,6 +34,14 @@ struct RowsArgs {
     int2* work_pen;         // [B][hist_cap] (id, scaled penalized logit as int bits)
     uint8_t* work_tmax;     // [B][TMAX] tile-max deficits
     uint8_t* work_anc;      // [B][NCK][256] checkpoint deficits below the thread's final max
+    // vocab shards (quasar_shard_*): this matrix holds global columns
+    // [col0, col0 + V); kernel A publishes per-row stats instead of finishing
+    // greedy rows, and the finishing kernel emits candidate keys
+    int64_t col0;
+    quasar_shard_stat* shard_stats;        // [B] out (kernel A), or NULL
+    const quasar_shard_stat* all_stats;    // [G][B] in (candidate and merge kernels)
+    int shard_G, shard_k, shard_rank;
+    uint64_t* shard_cand;                  // candidate kernel: [B][k] out; merge: [G][B][k] in
 };
 
 size_t rows_smem_bytes(int V);      // one-CTA-per-row kernel
@@ -43,5 +51,11 @@ size_t rows_workspace_bytes(int B, int hist_cap);  // device workspace of one la
 int rows_threads();
 // Launches kernel A (one streaming pass per row) and kernel B (cuts and draw).
 cudaError_t launch_sample_rows(const RowsArgs& args, void* workspace, cudaStream_t stream);
+// Vocab shards: kernel A alone (per-row stats into args.shard_stats), kernel
+// B in candidate mode (needs the same workspace), and the merge kernel.
+cudaError_t launch_shard_stats(const RowsArgs& args, void* workspace, cudaStream_t stream);
+cudaError_t launch_shard_candidates(const RowsArgs& args, void* workspace, cudaStream_t stream);
+size_t rows_merge_smem_bytes(int G, int k);
+cudaError_t launch_shard_merge(const RowsArgs& args, cudaStream_t stream);
 
 }  // namespace qs

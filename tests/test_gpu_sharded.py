@@ -1,0 +1,163 @@
+"""Vocab-sharded sampling on the GPU (quasar_shard_* through
+quasar_b200.VocabShardedSampler / CudaShardPhases), against the unsharded
+reference sampler on the full rows.
+
+* emulated shards: G column slices of one matrix on one GPU, the gathers done
+  by placing each shard's output at its rank's offset;
+* NCCL: two processes on two GPUs (skipped with fewer GPUs)."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests.helpers import V_FULL, assert_parity
+
+pytestmark = pytest.mark.gpu
+
+B, H, K = 64, 64, 40
+
+
+def _params(B):
+    prm = O.make_params(B, temperature=0.8, top_k=K, top_p=0.9, repeat_penalty=1.1)
+    prm["temperature"][::5] = 0.0     # greedy rows
+    prm["top_k"][1::5] = 1            # top_k = 1: one PRNG step, bit-exact id
+    prm["min_p"][2::5] = 0.05
+    prm["top_p"][3::5] = 1.0
+    return prm
+
+
+def _state(B):
+    seeds = np.arange(1, B + 1, dtype=np.uint64) * np.uint64(0x9E3779B97F4A7C15)
+    hist_len = np.full(B, H - 3, dtype=np.int32)
+    hist_head = (np.arange(B, dtype=np.int32) * 5) % H
+    return seeds, hist_len, hist_head
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def _check(ids, diag, rng_after, hist_after, len_after, logits_np, hist_np, prm, seeds, hist_len, hist_head):
+    import quasar_b200 as q
+    ref, ref_rng = O.pick_rows(logits_np, prm, seeds, hist=hist_np.copy(), hist_len=hist_len.copy(),
+                               hist_head=hist_head.copy())
+    assert_parity(ids, diag.view(q.DIAG_DTYPE).reshape(-1), rng_after.view(np.uint64), ref, ref_rng)
+    greedy = prm["temperature"] <= 0
+    assert np.array_equal(ids[greedy], ref["id"][greedy])
+    top1 = (prm["top_k"] == 1) & ~greedy
+    assert np.array_equal(ids[top1], ref["id"][top1])
+    for r in range(ids.size):
+        slot = (hist_head[r] + hist_len[r]) % H
+        assert hist_after[r, slot] == ids[r] and len_after[r] == hist_len[r] + 1
+
+
+@pytest.mark.parametrize("G", [2, 8])
+def test_emulated_shards_match_unsharded(G):
+    import torch
+    import quasar_b200 as q
+    from quasar_b200.sharded import STAT_BYTES, CudaShardPhases
+    from tests.helpers import gpu_inputs
+    logits, hist = gpu_inputs(O.SYNTH_NORMAL, 77, B, V_FULL, 3.0, H=H, hist_seed=78)
+    prm = _params(B)
+    seeds, hist_len, hist_head = _state(B)
+    dev = logits.device
+    d_params = q.params_to_device(prm, dev)
+    rng = torch.from_numpy(seeds.view(np.int64).copy()).to(dev)
+    th, tl = hist.clone(), torch.from_numpy(hist_len).to(dev)
+    thd = torch.from_numpy(hist_head).to(dev)
+    vs = V_FULL // G
+    ph = CudaShardPhases()
+    smp = q.VocabShardedSampler(K, phases=ph)
+    stream = torch.cuda.current_stream()
+    wsb = q.workspace_bytes(B, H)
+    wss = [torch.empty(wsb + 256, dtype=torch.uint8, device=dev) for _ in range(G)]
+    wss = [w[(-w.data_ptr()) % 256:][:wsb] for w in wss]
+    all_stats = torch.empty(G * B * STAT_BYTES, dtype=torch.uint8, device=dev)
+    all_cand = torch.empty(G * B * K, dtype=torch.int64, device=dev)
+    for g in range(G):
+        view = logits[:, g * vs:(g + 1) * vs]
+        ph.stats(view, g * vs, None, d_params, th, tl, thd, all_stats[g * B * STAT_BYTES:(g + 1) * B * STAT_BYTES],
+                 wss[g], stream)
+    for g in range(G):
+        view = logits[:, g * vs:(g + 1) * vs]
+        ph.candidates(view, g * vs, None, d_params, th, tl, thd, all_stats, G, g, K,
+                      all_cand[g * B * K:(g + 1) * B * K], wss[g], stream)
+    out = torch.empty(B, dtype=torch.int32, device=dev)
+    diag = torch.zeros(B, 4, dtype=torch.int32, device=dev)
+    ph.finish(all_cand, all_stats, G, K, B, None, d_params, rng, th, tl, thd, True, out, diag, stream)
+    torch.cuda.synchronize()
+    del smp
+    _check(out.cpu().numpy(), diag.cpu().numpy(), rng.cpu().numpy(), th.cpu().numpy(), tl.cpu().numpy(),
+           logits.cpu().numpy(), hist.cpu().numpy(), prm, seeds, hist_len, hist_head)
+
+
+def _free_port():
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]
+
+
+def _nccl_worker(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        import quasar_b200 as qb
+        vs = V_FULL // world
+        logits = torch.empty(B, vs, dtype=torch.float32, device=dev)
+        full = torch.empty(B, V_FULL, dtype=torch.float32, device=dev)
+        qb.synth_logits(qb.SYNTH_NORMAL, 79, 0, B, V_FULL, 3.0, full)
+        logits.copy_(full[:, rank * vs:(rank + 1) * vs])
+        hist = torch.empty(B, H, dtype=torch.int32, device=dev)
+        qb.synth_hist(80, 0, B, H, V_FULL, hist)
+        prm = _params(B)
+        seeds, hist_len, hist_head = _state(B)
+        rng = torch.from_numpy(seeds.view(np.int64).copy()).to(dev)
+        tl, thd = torch.from_numpy(hist_len).to(dev), torch.from_numpy(hist_head).to(dev)
+        diag = torch.zeros(B, 4, dtype=torch.int32, device=dev)
+        hist0 = hist.clone()
+        out = qb.VocabShardedSampler(K).pick(logits, rank * vs, rng, d_params=qb.params_to_device(prm, dev),
+                                             hist=hist, hist_len=tl, hist_head=thd, record=True, diag=diag)
+        torch.cuda.synchronize()
+        q.put((rank, out.cpu().numpy(), diag.cpu().numpy(), rng.cpu().numpy(), hist.cpu().numpy(),
+               tl.cpu().numpy(), hist0.cpu().numpy(), full.cpu().numpy() if rank == 0 else None))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gpu_nccl_matches_unsharded():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        r = q.get(timeout=300)
+        res[r[0]] = r[1:]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for a, b in zip(res[0][:5], res[1][:5]):
+        assert np.array_equal(a, b), "ranks disagree"
+    ids, diag, rng_after, hist_after, len_after, hist0, full = res[0]
+    seeds, hist_len, hist_head = _state(B)
+    _check(ids, diag, rng_after, hist_after, len_after, full, hist0, _params(B), seeds, hist_len, hist_head)
