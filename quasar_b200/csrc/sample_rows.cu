@@ -27,7 +27,7 @@
 // Two main kernels share the per-row code:
 //   sample_rows_tma  persistent CTAs of 8 consumer warps + 1 producer warp. The
 //                    producer streams the rows' 16 KB chunks with cp.async.bulk
-//                    (TMA, no multicast) into a 3-stage shared-memory ring
+//                    (TMA, this GPU's own memory only) into a 3-stage shared-memory ring
 //                    guarded by mbarriers, running ahead into the next row
 //                    while the consumers finish the current one. Needs rows
 //                    that start 16-byte aligned and V % 4 == 0.
