@@ -320,6 +320,86 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+def run_vocab_sharded(args) -> None:
+    """Config 4: the vocab split over the ranks (tensor-parallel LM head).
+
+    Every rank holds V/N columns of the same 8192 rows (N(0,3), seeded);
+    top_k 40, top_p 0.9, temperature 0.8, no history. One step = one
+    VocabShardedSampler.pick: per-shard stats, an NCCL all-gather, per-shard
+    top-40 candidates, a second all-gather, merge/cut/draw on every rank.
+    `value` = rows per second of the whole job (all ranks sample the same
+    rows together); the roofline counts each rank's shard bytes against one
+    GPU's measured bandwidth."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev, world_size=world,
+                            rank=rank, init_method=None if world > 1 else "tcp://127.0.0.1:29611")
+    import quasar_b200 as q
+    rows, K = 8192, 40
+    vs = V // world
+    full = torch.empty(rows, V, dtype=torch.float32, device=dev)
+    q.synth_logits(q.SYNTH_NORMAL, SEED_LOGITS, 0, rows, V, 3.0, full)
+    shard = full[:, rank * vs:(rank + 1) * vs].contiguous()
+    del full
+    torch.cuda.empty_cache()
+    seeds = np.arange(rows, dtype=np.uint64) + np.uint64(SEED_RNG)
+    rng = torch.from_numpy(seeds.view(np.int64).copy()).to(dev)
+    out = torch.empty(rows, dtype=torch.int32, device=dev)
+    smp = q.VocabShardedSampler(K)
+    prm = {"temperature": 0.8, "top_k": K, "top_p": 0.9}
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        smp.pick(shard, rank * vs, rng, params=prm, out=out, stream=stream)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(",".join(str(i) for i in range(world)))
+    if rank == 0:
+        clocks.start()
+        time.sleep(0.2)
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    clk = clocks.stop() if rank == 0 else None
+    per_step = ms / 1e3 / args.steps
+    shard_bytes = rows * (vs * 4 + 24)
+    peak, peak_kind = peak_hbm()
+    line = {"metric": "sampled rows/s, vocab-sharded (config 4)", "value": rows / per_step, "unit": "rows/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": "config4: %d rows x %d columns per GPU, N(0,3), top_k 40, top_p 0.9, T 0.8"
+                                   % (rows, vs), "global_batch": rows, "parallelism": "vocab x%d" % world},
+            "roofline": {"bound": "hbm", "achieved": shard_bytes / per_step / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": shard_bytes / per_step / 1e9 / peak, "traffic": None, "peak_source": peak_kind,
+                         "algorithmic_bytes_per_launch": shard_bytes},
+            "gpu_launches": args.steps * 3, "clocks": clk}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -330,9 +410,13 @@ def main() -> None:
     ap.add_argument("--rows", type=int, default=B, help="rows per GPU (profiling runs use fewer)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg (profiling)")
     ap.add_argument("--flags", type=int, default=0, help="quasar_sampler_pick_batch flags (A/B runs)")
+    ap.add_argument("--mode", default="rows", choices=["rows", "vocab"],
+                    help="rows: config 3, rows split over GPUs (default); vocab: config 4, vocab split")
     args = ap.parse_args()
     globals()["B"] = args.rows
-    if args.impl == "reference":
+    if args.mode == "vocab" and args.impl == "ours":
+        run_vocab_sharded(args)
+    elif args.impl == "reference":
         run_reference_arm(args)
     else:
         run_ours(args)
