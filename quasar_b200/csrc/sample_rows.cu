@@ -876,6 +876,15 @@ struct LdgSource {
     __device__ __forceinline__ void release() {}
 };
 
+// The slow side of a ring wait: the chunk has not landed yet. Gives up at
+// once after an abort, else waits (bounded) and records a timeout as one.
+__device__ __noinline__ bool ring_wait_slow(uint32_t bar, uint32_t par, int* abort_flag) {
+    if (*reinterpret_cast<volatile int*>(abort_flag)) return false;
+    if (mbar_wait(bar, par)) return true;
+    *reinterpret_cast<volatile int*>(abort_flag) = 1;
+    return false;
+}
+
 struct TmaSource {
     static constexpr bool kRegs = false;
     const float* ring;  // NSTAGE tiles
@@ -885,11 +894,9 @@ struct TmaSource {
     __device__ __forceinline__ void get(const Row& R, int it, float (&v)[16], Shared& s) {
         const int st = (int)(g % NSTAGE);
         const uint32_t par = (g / NSTAGE) & 1u;
-        bool ok = *reinterpret_cast<volatile int*>(&s.abort) == 0;
-        if (ok && !mbar_wait(full0 + 8u * st, par)) {
-            s.abort = 1;
-            ok = false;
-        }
+        // a landed chunk is valid whatever else happened; only a chunk that
+        // has not landed consults the abort flag
+        const bool ok = mbar_try_wait(full0 + 8u * st, par) || ring_wait_slow(full0 + 8u * st, par, &s.abort);
         const int tid = threadIdx.x;
         const float* t = ring + st * TILE_ELEMS;
         const int e0 = it * TILE_ELEMS + 8 * tid, e1 = e0 + 8 * CONSUMERS;
