@@ -1,0 +1,104 @@
+"""Full-size batches (BASELINE.json configs 3 and 5) on the GPU, checked
+through properties that do not depend on the batch size, plus oracle parity
+on an evenly spread subset of rows (their inputs regenerated on the CPU from
+the same counter-based recipe, bit for bit):
+
+* every id is a column index; every stochastic row advanced its PRNG by
+  exactly one xorshift64* step (sample.c:72-81), bit-exact;
+* the ring got the chosen id where sample.c:83-92 puts it (full rings
+  overwrite the oldest entry and advance the head);
+* every row took the candidate path, kept >= 1 token, and the chosen token's
+  p is at or above the min-p floor min_p * p_max (sample.c:162-167);
+* the subset matches the reference sampler under the stated tolerance."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests.helpers import V_FULL, assert_parity
+
+pytestmark = pytest.mark.gpu
+
+M64 = (1 << 64) - 1
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def _xorshift_once(seeds):
+    x = seeds.astype(np.uint64).copy()
+    x ^= x << np.uint64(13)
+    x ^= x >> np.uint64(7)
+    x ^= x << np.uint64(17)
+    return x
+
+
+def _run(kind, scale, seed, B, H, hist_seed, temps, prm, seeds):
+    import torch
+    import quasar_b200 as q
+    dev = torch.device("cuda")
+    logits = torch.empty(B, V_FULL, dtype=torch.float32, device=dev)
+    q.synth_logits(kind, seed, 0, B, V_FULL, scale, logits)
+    hist = torch.empty(B, H, dtype=torch.int32, device=dev)
+    q.synth_hist(hist_seed, 0, B, H, V_FULL, hist)
+    hist0 = hist.cpu().numpy()
+    head0 = (np.arange(B, dtype=np.int32) * 3) % H
+    hist_len = torch.full((B,), H, dtype=torch.int32, device=dev)   # full rings
+    hist_head = torch.from_numpy(head0).to(dev)
+    rng = torch.from_numpy(seeds.view(np.int64).copy()).to(dev)
+    diag = torch.zeros(B, 4, dtype=torch.int32, device=dev)
+    out = q.pick_batch(logits, rng, d_params=q.params_to_device(prm, dev), hist=hist, hist_len=hist_len,
+                       hist_head=hist_head, record=True, diag=diag)
+    torch.cuda.synchronize()
+    res = dict(ids=out.cpu().numpy(), diag=diag.cpu().numpy().view(q.DIAG_DTYPE).reshape(B),
+               rng=rng.cpu().numpy().view(np.uint64), hist=hist.cpu().numpy(), hist0=hist0,
+               head0=head0, head1=hist_head.cpu().numpy(), len1=hist_len.cpu().numpy())
+    del logits
+    torch.cuda.empty_cache()
+    return res
+
+
+def _properties(r, prm, seeds, H):
+    ids, d = r["ids"], r["diag"]
+    B = ids.size
+    assert ((ids >= 0) & (ids < V_FULL)).all()
+    assert np.array_equal(r["rng"], _xorshift_once(seeds))
+    rows = np.arange(B)
+    assert np.array_equal(r["hist"][rows, r["head0"]], ids)
+    assert np.array_equal(r["head1"], (r["head0"] + 1) % H) and (r["len1"] == H).all()
+    assert (d["path"] == 1).all(), np.bincount(d["path"])
+    assert (d["n_kept"] >= 1).all()
+    assert ((d["inv_sum"] > 0) & (d["inv_sum"] <= 1)).all()
+    floor = prm["min_p"] * d["inv_sum"]
+    assert (d["p_chosen"] >= floor * (1 - 1e-6)).all()
+
+
+def _subset_parity(r, kind, scale, seed, hist_seed, H, prm, seeds, step):
+    rows = np.arange(0, r["ids"].size, step)
+    logits = np.concatenate([O.synth_logits(kind, seed, int(i), 1, V_FULL, scale) for i in rows])
+    hist = r["hist0"][rows]
+    res, rng_ref = O.pick_rows(logits, prm[rows], seeds[rows], hist=hist,
+                               hist_len=np.full(rows.size, H, np.int32), hist_head=r["head0"][rows])
+    assert_parity(r["ids"][rows], r["diag"][rows], r["rng"][rows], res, rng_ref)
+
+
+def test_config3_full_batch():
+    B, H = 4096, 256
+    temps = O.synth_uniform(3, 0, B, 0.2, 1.5)
+    prm = O.make_params(B, temperature=temps, top_p=0.95, min_p=0.05, repeat_penalty=1.1)
+    seeds = np.arange(B, dtype=np.uint64) + np.uint64(5000)
+    r = _run(O.SYNTH_NORMAL, 3.0, 3, B, H, 33, temps, prm, seeds)
+    _properties(r, prm, seeds, H)
+    _subset_parity(r, O.SYNTH_NORMAL, 3.0, 3, 33, H, prm, seeds, 64)
+
+
+def test_config5_full_batch():
+    B, H = 16384, 2048
+    prm = O.make_params(B, temperature=1.0, top_p=1.0, min_p=0.1, repeat_penalty=1.3)
+    seeds = np.arange(B, dtype=np.uint64) + np.uint64(9000)
+    r = _run(O.SYNTH_ZIPF, 1.1, 5, B, H, 55, None, prm, seeds)
+    _properties(r, prm, seeds, H)
+    _subset_parity(r, O.SYNTH_ZIPF, 1.1, 5, 55, H, prm, seeds, 512)
