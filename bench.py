@@ -42,12 +42,23 @@ BYTES_PER_ROW = V * 4 + H * 4 + 60
 FALLBACK_HBM_GBS = 6650.0
 
 
+# Rows-mode workloads: 3 is the headline, 5 the
+# full-vocab softmax + multinomial case.
+CONFIGS = {
+    3: dict(rows=4096, hist=256, kind=0, scale=3.0, temp=(0.2, 1.5), top_p=0.95, min_p=0.05, rp=1.1,
+            text="config3: N(0,3) logits, per-row T~U[0.2,1.5], top_p 0.95, min_p 0.05, "
+                 "repeat_penalty 1.1 over 256 history ids, record on"),
+    5: dict(rows=16384, hist=2048, kind=2, scale=1.1, temp=(1.0, 1.0), top_p=1.0, min_p=0.1, rp=1.3,
+            text="config5: Zipf(1.1) logits (-1.1 ln rank, per-row rank permutation), T 1.0, min_p 0.1, "
+                 "repeat_penalty 1.3 over 2048 history ids, record on"),
+}
+CFG = CONFIGS[3]
+
+
 def workload_config(n_gpus: int) -> dict:
-    return {"workload": "config3: N(0,3) logits, per-row T~U[0.2,1.5], top_p 0.95, min_p 0.05, "
-                        "repeat_penalty 1.1 over 256 history ids, record on",
-            "rows_per_gpu": B, "vocab": V, "history": H, "global_batch": B * n_gpus,
+    return {"workload": CFG["text"], "rows_per_gpu": B, "vocab": V, "history": H, "global_batch": B * n_gpus,
             "parallelism": f"rows x{n_gpus}",
-            "l2": "inputs larger than L2 (2.49 GB of logits per step per GPU)"}
+            "l2": "inputs larger than L2 (%.2f GB of logits per step per GPU)" % (B * V * 4 / 1e9)}
 
 
 def peak_hbm() -> tuple[float, str]:
@@ -139,12 +150,13 @@ def cpu_threads() -> int:
 
 
 def cpu_rows(n_rows: int, row0: int = 0):
-    """Config-3 rows [row0, row0+n_rows) generated on the CPU (same bits as the GPU)."""
+    """Workload rows [row0, row0+n_rows) generated on the CPU (same bits as the GPU)."""
     from oracle import oracle as O
-    logits = O.synth_logits(O.SYNTH_NORMAL, SEED_LOGITS, row0, n_rows, V, 3.0)
+    logits = O.synth_logits(CFG["kind"], SEED_LOGITS, row0, n_rows, V, CFG["scale"])
     hist = O.synth_hist(SEED_HIST, row0, n_rows, H, V)
-    temps = O.synth_uniform(SEED_TEMP, row0, n_rows, 0.2, 1.5)
-    prm = O.make_params(n_rows, temperature=temps, top_p=0.95, min_p=0.05, repeat_penalty=1.1)
+    temps = O.synth_uniform(SEED_TEMP, row0, n_rows, *CFG["temp"])
+    prm = O.make_params(n_rows, temperature=temps, top_p=CFG["top_p"], min_p=CFG["min_p"],
+                        repeat_penalty=CFG["rp"])
     seeds = np.arange(row0, row0 + n_rows, dtype=np.uint64) + np.uint64(SEED_RNG)
     return logits, hist, prm, seeds
 
@@ -214,13 +226,13 @@ def run_ours(args) -> None:
 
     row0 = rank * B  # each rank samples its own rows of the synthetic batch
     logits = torch.empty(B, V, dtype=torch.float32, device=dev)
-    q.synth_logits(q.SYNTH_NORMAL, SEED_LOGITS, row0, B, V, 3.0, logits)
+    q.synth_logits(CFG["kind"], SEED_LOGITS, row0, B, V, CFG["scale"], logits)
     hist = torch.empty(B, H, dtype=torch.int32, device=dev)
     q.synth_hist(SEED_HIST, row0, B, H, V, hist)
     temps = torch.empty(B, dtype=torch.float32, device=dev)
-    q.synth_uniform(SEED_TEMP, row0, B, 0.2, 1.5, temps)
-    prm = q.make_params(B, temperature=temps.cpu().numpy(), top_p=0.95, min_p=0.05,
-                        repeat_penalty=1.1)
+    q.synth_uniform(SEED_TEMP, row0, B, *CFG["temp"], temps)
+    prm = q.make_params(B, temperature=temps.cpu().numpy(), top_p=CFG["top_p"], min_p=CFG["min_p"],
+                        repeat_penalty=CFG["rp"])
     d_params = q.params_to_device(prm, dev)
     seeds = np.arange(row0, row0 + B, dtype=np.uint64) + np.uint64(SEED_RNG)
     rng = torch.from_numpy(seeds.view(np.int64).copy()).to(dev)
@@ -292,7 +304,8 @@ def run_ours(args) -> None:
     per_launch_s = (ms / 1e3) / args.steps  # one kernel launch per step
     achieved = B * BYTES_PER_ROW / per_launch_s / 1e9
     peak, peak_kind = peak_hbm()
-    traffic = ncu_traffic_per_launch()
+    # the committed ncu summary covers the headline workload only
+    traffic = ncu_traffic_per_launch() if CFG is CONFIGS[3] and B == CONFIGS[3]["rows"] else None
     line = {"metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -407,13 +420,20 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--rows", type=int, default=B, help="rows per GPU (profiling runs use fewer)")
+    ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS),
+                    help="rows-mode workload: BASELINE.json config 3 (headline) or 5")
+    ap.add_argument("--rows", type=int, default=None, help="rows per GPU (default: the config's; profiling "
+                                                          "runs use fewer)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg (profiling)")
     ap.add_argument("--flags", type=int, default=0, help="quasar_sampler_pick_batch flags (A/B runs)")
     ap.add_argument("--mode", default="rows", choices=["rows", "vocab"],
                     help="rows: config 3, rows split over GPUs (default); vocab: config 4, vocab split")
     args = ap.parse_args()
-    globals()["B"] = args.rows
+    cfg = CONFIGS[args.config]
+    globals()["CFG"] = cfg
+    globals()["B"] = args.rows or cfg["rows"]
+    globals()["H"] = cfg["hist"]
+    globals()["BYTES_PER_ROW"] = V * 4 + cfg["hist"] * 4 + 60
     if args.mode == "vocab" and args.impl == "ours":
         run_vocab_sharded(args)
     elif args.impl == "reference":
