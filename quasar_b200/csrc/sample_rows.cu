@@ -37,6 +37,8 @@
 // rows report id -1 and the kernel runs to its end.
 #include <math.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "sample_rows.cuh"
 
@@ -891,6 +893,9 @@ struct TmaSource {
     uint32_t full0, empty0;
     uint32_t g;  // chunks consumed by this CTA so far
     __device__ __forceinline__ void begin(const Row&) {}
+    // kMaybeLast = false: the caller knows `it` is not the row's last chunk
+    // (the only partial one), so no bounds mask is needed
+    template <bool kMaybeLast = true>
     __device__ __forceinline__ void get(const Row& R, int it, float (&v)[16], Shared& s) {
         const int st = (int)(g % NSTAGE);
         const uint32_t par = (g / NSTAGE) & 1u;
@@ -909,7 +914,7 @@ struct TmaSource {
             v[8] = c.x; v[9] = c.y; v[10] = c.z; v[11] = c.w;
             v[12] = d.x; v[13] = d.y; v[14] = d.z; v[15] = d.w;
         }
-        if (!ok || it == R.ntiles - 1) {  // only the last chunk of a row is partial
+        if (!ok || (kMaybeLast && it == R.ntiles - 1)) {  // only the last chunk of a row is partial
 #pragma unroll
             for (int k = 0; k < 8; k++) {
                 if (!ok || e0 + k >= R.V) v[k] = -INFINITY;
@@ -1036,17 +1041,22 @@ __device__ __forceinline__ void stream_tiles(const Row& R, Src& src, Shared& s, 
         Src::load(R, 0, va);
         for (int it = 0; it < R.ntiles; it += 2) {
             if (it + 1 < R.ntiles) Src::load(R, it + 1, vb);
-            body(va, it);
+            body(va, it, std::true_type());
             if (it + 2 < R.ntiles) Src::load(R, it + 2, va);
-            if (it + 1 < R.ntiles) body(vb, it + 1);
+            if (it + 1 < R.ntiles) body(vb, it + 1, std::true_type());
         }
     } else {
-        for (int it = 0; it < R.ntiles; it++) {
+        // every chunk but the last is full: its checks are compile-time
+        for (int it = 0; it + 1 < R.ntiles; it++) {
             float v[16];
-            src.get(R, it, v, s);
+            src.template get<false>(R, it, v, s);
             src.release();
-            body(v, it);
+            body(v, it, std::false_type());
         }
+        float v[16];
+        src.template get<true>(R, R.ntiles - 1, v, s);
+        src.release();
+        body(v, R.ntiles - 1, std::true_type());
     }
 }
 
@@ -1217,7 +1227,9 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
     const f32x2 inv_t2 = pack2(R.inv_t, R.inv_t);
     float m = -INFINITY;
     double S = 0.0;
-    auto body = [&](float (&v)[16], int it) {
+    // last: std::true_type when `it` may be the row's last tile
+    auto body = [&](float (&v)[16], int it, auto last) {
+        constexpr bool kMaybeLast = decltype(last)::value;
         if (R.use_pen) mask_penalized(R, bits8, s.pen_lut, v, it * OCT_TILE + tid, it * OCT_TILE + tid + CONSUMERS);
         // sample.c:142: sc = l * inv_t, rounded exactly like the reference
         // (packed pairs: each lane is the same IEEE multiply)
@@ -1265,17 +1277,17 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
         }
         if (g == 1) {
             tword |= deficit_byte(m, mt) << (8 * (it & 3));
-            if ((it & 3) == 3 || it == R.ntiles - 1) {
+            if ((it & 3) == 3 || (kMaybeLast && it == R.ntiles - 1)) {
                 tmax32[(it >> 2) * CONSUMERS + tid] = tword;
                 tword = 0u;
             }
             if (it < 32 && ((it + 1) & it) == 0) anc_s[__popc(it) * CONSUMERS + tid] = m;
         } else {
             slotmax = fmaxf(slotmax, mt);
-            if (it % g == g - 1 || it == R.ntiles - 1) {
+            if (it % g == g - 1 || (kMaybeLast && it == R.ntiles - 1)) {
                 const int sl = it / g;
                 tword |= deficit_byte(m, slotmax) << (8 * (sl & 3));
-                if ((sl & 3) == 3 || it == R.ntiles - 1) {
+                if ((sl & 3) == 3 || (kMaybeLast && it == R.ntiles - 1)) {
                     tmax32[(sl >> 2) * CONSUMERS + tid] = tword;
                     tword = 0u;
                 }
