@@ -35,6 +35,7 @@
 //                    prefetch; any alignment and V.
 // Every mbarrier wait is bounded (clock64); a timeout sets the abort flag, the
 // rows report id -1 and the kernel runs to its end.
+#include <float.h>
 #include <math.h>
 
 #include <type_traits>
@@ -1225,78 +1226,95 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
     uint32_t tword = 0u;  // four slot bytes of this thread, stored together (tbl_off layout)
     float slotmax = -INFINITY;
     const f32x2 inv_t2 = pack2(R.inv_t, R.inv_t);
-    float m = -INFINITY;
+    // the running max starts finite, so every term is exp(sc - m) with x <= 0
+    // from the first tile on (an all -inf stretch adds exp(-inf) = 0)
+    float m = -FLT_MAX;
     double S = 0.0;
-    // last: std::true_type when `it` may be the row's last tile
-    auto body = [&](float (&v)[16], int it, auto last) {
-        constexpr bool kMaybeLast = decltype(last)::value;
-        if (R.use_pen) mask_penalized(R, bits8, s.pen_lut, v, it * OCT_TILE + tid, it * OCT_TILE + tid + CONSUMERS);
-        // sample.c:142: sc = l * inv_t, rounded exactly like the reference
-        // (packed pairs: each lane is the same IEEE multiply)
-        f32x2 sc2[8];
-        float sc[16];
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            sc2[j] = mul2(pack2(v[2 * j], v[2 * j + 1]), inv_t2);
-            unpack2(sc2[j], sc[2 * j], sc[2 * j + 1]);
-        }
-        const float mt = fmaxf(max3(max3(sc[0], sc[1], sc[2]), max3(sc[3], sc[4], sc[5]),
-                                    max3(sc[6], sc[7], sc[8])),
-                               max3(max3(sc[9], sc[10], sc[11]), max3(sc[12], sc[13], sc[14]), sc[15]));
-        if (mt > m) {
-            S *= exp((double)m - (double)mt);
-            m = mt;
-        }
-        if (m > -INFINITY) {
-            // sample.c:148 against the running max: x = sc - m, then the term
-            f32x2 e[8];
-            const f32x2 nm2 = pack2(-m, -m);
+    int next_ck = 0, ck = 0;  // next checkpoint slot (0, 1, 3, 7, 15, 31) and its index
+    // g1: one tile per table slot (compile-time); last: std::true_type when
+    // `it` may be the row's last tile
+    auto run = [&](auto g1) {
+        constexpr bool kG1 = decltype(g1)::value;
+        auto body = [&](float (&v)[16], int it, auto last) {
+            constexpr bool kMaybeLast = decltype(last)::value;
+            if (R.use_pen)
+                mask_penalized(R, bits8, s.pen_lut, v, it * OCT_TILE + tid, it * OCT_TILE + tid + CONSUMERS);
+            // sample.c:142: sc = l * inv_t, rounded exactly like the reference
+            // (packed pairs: each lane is the same IEEE multiply)
+            f32x2 sc2[8];
+            float sc[16];
 #pragma unroll
             for (int j = 0; j < 8; j++) {
+                sc2[j] = mul2(pack2(v[2 * j], v[2 * j + 1]), inv_t2);
+                unpack2(sc2[j], sc[2 * j], sc[2 * j + 1]);
+            }
+            const float mt = fmaxf(max3(max3(sc[0], sc[1], sc[2]), max3(sc[3], sc[4], sc[5]),
+                                        max3(sc[6], sc[7], sc[8])),
+                                   max3(max3(sc[9], sc[10], sc[11]), max3(sc[12], sc[13], sc[14]), sc[15]));
+            if (mt > m) {
+                S *= exp((double)m - (double)mt);
+                m = mt;
+            }
+            {
+                // sample.c:148 against the running max: x = sc - m, then the term
+                f32x2 e[8];
+                const f32x2 nm2 = pack2(-m, -m);
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
 #if QS_SUM_EXP == 3
-                e[j] = exp_fast2(add2(sc2[j], nm2));
-#elif QS_SUM_EXP == 2 || QS_SUM_EXP == 4
-                if (QS_SUM_EXP == 4 && (j & 1) == 0) {
                     e[j] = exp_fast2(add2(sc2[j], nm2));
-                } else {
-                    float x0, x1;
-                    unpack2(add2(sc2[j], nm2), x0, x1);
-                    e[j] = exp_poly2(x0, x1);
-                }
+#elif QS_SUM_EXP == 2 || QS_SUM_EXP == 4
+                    if (QS_SUM_EXP == 4 && (j & 1) == 0) {
+                        e[j] = exp_fast2(add2(sc2[j], nm2));
+                    } else {
+                        float x0, x1;
+                        unpack2(add2(sc2[j], nm2), x0, x1);
+                        e[j] = exp_poly2(x0, x1);
+                    }
 #else
-                e[j] = pack2(sum_term_exp(__fsub_rn(sc[2 * j], m)), sum_term_exp(__fsub_rn(sc[2 * j + 1], m)));
+                    e[j] = pack2(sum_term_exp(__fsub_rn(sc[2 * j], m)),
+                                 sum_term_exp(__fsub_rn(sc[2 * j + 1], m)));
 #endif
-            }
+                }
 #pragma unroll
-            for (int w = 4; w > 0; w >>= 1)
+                for (int w = 4; w > 0; w >>= 1)
 #pragma unroll
-                for (int j = 0; j < w; j++) e[j] = add2(e[j], e[j + w]);
-            float e0, e1;
-            unpack2(e[0], e0, e1);
-            S += (double)(e0 + e1);
-        }
-        if (g == 1) {
-            tword |= deficit_byte(m, mt) << (8 * (it & 3));
-            if ((it & 3) == 3 || (kMaybeLast && it == R.ntiles - 1)) {
-                tmax32[(it >> 2) * CONSUMERS + tid] = tword;
-                tword = 0u;
+                    for (int j = 0; j < w; j++) e[j] = add2(e[j], e[j + w]);
+                float e0, e1;
+                unpack2(e[0], e0, e1);
+                S += (double)(e0 + e1);
             }
-            if (it < 32 && ((it + 1) & it) == 0) anc_s[__popc(it) * CONSUMERS + tid] = m;
-        } else {
-            slotmax = fmaxf(slotmax, mt);
-            if (it % g == g - 1 || (kMaybeLast && it == R.ntiles - 1)) {
-                const int sl = it / g;
-                tword |= deficit_byte(m, slotmax) << (8 * (sl & 3));
-                if ((sl & 3) == 3 || (kMaybeLast && it == R.ntiles - 1)) {
-                    tmax32[(sl >> 2) * CONSUMERS + tid] = tword;
+            if constexpr (kG1) {
+                tword |= deficit_byte(m, mt) << (8 * (it & 3));
+                if ((it & 3) == 3 || (kMaybeLast && it == R.ntiles - 1)) {
+                    tmax32[(it >> 2) * CONSUMERS + tid] = tword;
                     tword = 0u;
                 }
-                if (sl < 32 && ((sl + 1) & sl) == 0) anc_s[__popc(sl) * CONSUMERS + tid] = m;
-                slotmax = -INFINITY;
+                if (it == next_ck) {  // checkpoints are tiles 0, 1, 3, 7, 15, 31
+                    anc_s[ck * CONSUMERS + tid] = m;
+                    next_ck = ++ck < NCK ? 2 * next_ck + 1 : -1;
+                }
+            } else {
+                slotmax = fmaxf(slotmax, mt);
+                if (it % g == g - 1 || (kMaybeLast && it == R.ntiles - 1)) {
+                    const int sl = it / g;
+                    tword |= deficit_byte(m, slotmax) << (8 * (sl & 3));
+                    if ((sl & 3) == 3 || (kMaybeLast && it == R.ntiles - 1)) {
+                        tmax32[(sl >> 2) * CONSUMERS + tid] = tword;
+                        tword = 0u;
+                    }
+                    if (sl == next_ck) {
+                        anc_s[ck * CONSUMERS + tid] = m;
+                        next_ck = ++ck < NCK ? 2 * next_ck + 1 : -1;
+                    }
+                    slotmax = -INFINITY;
+                }
             }
-        }
+        };
+        stream_tiles(R, src, s, body);
     };
-    stream_tiles(R, src, s, body);
+    if (g == 1) run(std::true_type());
+    else run(std::false_type());
     if (R.use_pen) {
         csync();
         // the penalized elements join the running max and sum exactly, and
