@@ -638,86 +638,6 @@ __device__ void candidate_cuts(const uint64_t* keys, int nk, const RowParams& P,
     csync();
 }
 
-__device__ __forceinline__ void cx_desc(uint64_t& a, uint64_t& b, bool desc) {
-    const uint64_t hi = a > b ? a : b, lo = a > b ? b : a;
-    a = desc ? hi : lo;
-    b = desc ? lo : hi;
-}
-
-// Bitonic sort, descending, of n2 = 256*E keys held E per lane: warp w owns
-// positions w*C + q*32 + lane (C = 32*E, q < E). Exchanges across lanes use
-// shuffles, across a lane's own registers plain compares, and only exchanges
-// across warps go through shared memory (sm) and the consumer barrier.
-template <int E>
-__device__ void sort_regs_desc(uint64_t (&v)[E], uint64_t* sm) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    constexpr int C = 32 * E;
-    constexpr int N2 = CONSUMERS * E;
-    for (int k = 2; k <= N2; k <<= 1) {
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            if (j >= C) {
-#pragma unroll
-                for (int q = 0; q < E; q++) sm[w * C + q * 32 + lane] = v[q];
-                csync();
-#pragma unroll
-                for (int q = 0; q < E; q++) {
-                    const int i = w * C + q * 32 + lane;
-                    const uint64_t x = sm[i ^ j];
-                    const bool first = (i & j) == 0, desc = (i & k) == 0;
-                    const uint64_t hi = v[q] > x ? v[q] : x, lo = v[q] > x ? x : v[q];
-                    v[q] = (first == desc) ? hi : lo;
-                }
-                csync();
-            } else if (j >= 32) {
-                const int jb = j >> 5;
-#pragma unroll
-                for (int q = 0; q < E; q++) {
-#pragma unroll
-                    for (int b = 1; b < E; b <<= 1) {
-                        if (b == jb && (q & b) == 0) {
-                            const int i = w * C + q * 32 + lane;
-                            cx_desc(v[q], v[q | b], (i & k) == 0);
-                        }
-                    }
-                }
-            } else {
-#pragma unroll
-                for (int q = 0; q < E; q++) {
-                    const int i = w * C + q * 32 + lane;
-                    const uint64_t x = __shfl_xor_sync(FULL, v[q], j);
-                    const bool first = (lane & j) == 0, desc = (i & k) == 0;
-                    const uint64_t hi = v[q] > x ? v[q] : x, lo = v[q] > x ? x : v[q];
-                    v[q] = (first == desc) ? hi : lo;
-                }
-            }
-        }
-    }
-}
-
-// Converts the nk raw (sc, id) entries raw[0, nk) into (p, ~id) keys, sorts
-// them descending and leaves them in buf[0, 256*E) (zero keys past nk).
-template <int E>
-__device__ void keys_sorted(uint64_t* buf, const uint64_t* raw, int nk, const Row& R) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    constexpr int C = 32 * E;
-    uint64_t v[E];
-#pragma unroll
-    for (int q = 0; q < E; q++) {
-        const int i = w * C + q * 32 + lane;
-        v[q] = 0ull;
-        if (i < nk) {
-            const uint64_t e = raw[i];
-            const float sc = __uint_as_float((uint32_t)(e >> 32));
-            v[q] = ((uint64_t)p_key(sc, R.M, R.thr, R.inv) << 32) | (uint32_t)(~(uint32_t)e);
-        }
-    }
-    csync();  // every raw entry is in registers before buf is reused
-    sort_regs_desc<E>(v, buf);
-#pragma unroll
-    for (int q = 0; q < E; q++) buf[w * C + q * 32 + lane] = v[q];
-    csync();
-}
-
 // Tile-max table entry: how far (in 1/8 nat, rounded down, saturating at 255)
 // a slot's max lies below the thread's running max m at the slot's end. Since
 // m only grows, slot max <= (thread's final max) - d/8 holds at the end.
@@ -730,11 +650,6 @@ __device__ __forceinline__ uint8_t tile_deficit(float m, float slotmax) {
 __device__ __forceinline__ uint32_t deficit_byte(float m, float slotmax) {
     return __float2uint_rd(fminf(__fmul_rd(__fsub_rd(m, slotmax), 8.0f), 255.0f));
 }
-// Upper bound of a slot's max from its entry and its thread's final max.
-__device__ __forceinline__ float tile_bound(float thread_max, uint32_t d) {
-    return __fsub_ru(thread_max, 0.125f * (float)d);
-}
-
 // Lower bound of the k-th largest scaled logit of the row (k <= 256): the
 // k-th largest of the 256 per-thread maxima (256 distinct elements), lowered by
 // a margin that covers ties in p. Rank by (value desc, thread asc).
@@ -1115,14 +1030,6 @@ __device__ __forceinline__ void claim_penalized(const RowCtx& c, const Row& R, u
             const uint32_t bit = 1u << (id & 31);
             if (atomicAnd(&bits[id >> 5], ~bit) & bit) f(id, penalize(__ldg(R.ptr + id), R.rp));
         }
-    }
-}
-
-// Sets the bits of the row's history ids again (after claim_penalized).
-__device__ __forceinline__ void set_bits(const RowCtx& c, const Row& R, uint32_t* bits) {
-    for (int i = threadIdx.x; i < c.len; i += CONSUMERS) {
-        const int id = ring_id(c, i);
-        if (id >= 0 && id < R.V) atomicOr(&bits[id >> 5], 1u << (id & 31));
     }
 }
 
