@@ -86,8 +86,8 @@ struct Hist {
 constexpr int FINISH_SCRATCH = (int)sizeof(Hist) > CAP * 8 ? (int)sizeof(Hist) : CAP * 8;
 
 // Counting sort of the candidate keys (kernel B): NBK buckets of the p key's
-// bits below the row's largest key, four per consumer thread.
-constexpr int NBK = 1024;
+// bits below the row's largest key, two per consumer thread.
+constexpr int NBK = 512;
 constexpr int BK_MAX = 256;  // largest bucket the in-bucket ranking takes
 struct Buckets {
     uint32_t cnt[NBK];
@@ -110,11 +110,15 @@ struct Shared {
     float pf_lo, pf_hi;
     int res_id, res_nc, res_pos;
     float res_p;
-    float4 pen_lut[16];   // nibble n -> +0 / -inf per bit (penalized elements leave the stream)
     int cut_p, cut_m, cut_d;  // candidate cuts (atomicMin targets)
     int big_bucket;           // a bucket of the counting sort exceeds BK_MAX
     uint32_t bk_hi[CWARPS];   // per-warp maxima of the counting sort's keys
     double rsum;
+};
+
+// Kernel A's shared state: the common slots plus the penalty mask table.
+struct SharedA : Shared {
+    float4 pen_lut[16];   // nibble n -> +0 / -inf per bit (penalized elements leave the stream)
 };
 
 // Barrier of the 256 consumer threads (warps 0-7); the TMA producer warp never
@@ -717,7 +721,7 @@ __device__ const uint64_t* bucket_sort_keys(uint64_t* buf, int nk, const Row& R,
         atomicAdd(&bk->cnt[(kmax - (uint32_t)(src[i] >> 32)) >> sh], 1u);
     csync();
     {
-        // exclusive scan of the counts: thread t owns buckets 4t .. 4t+3
+        // exclusive scan of the counts: thread t owns buckets PER*t .. PER*t+PER-1
         constexpr int PER = NBK / CONSUMERS;
         uint32_t c[PER], tot = 0u;
 #pragma unroll
@@ -996,7 +1000,7 @@ __device__ __forceinline__ void mask_penalized(const Row& R, const uint8_t* bits
     }
 }
 
-__device__ __forceinline__ void init_pen_lut(Shared& s) {
+__device__ __forceinline__ void init_pen_lut(SharedA& s) {
     if (threadIdx.x < 16) {
         const int n = threadIdx.x;
         s.pen_lut[n] = make_float4((n & 1) ? -INFINITY : 0.0f, (n & 2) ? -INFINITY : 0.0f,
@@ -1047,7 +1051,7 @@ __device__ __forceinline__ void claim_penalized(const RowCtx& c, const Row& R, u
 // first checkpoint >= j + slot deficit)/8: tight for early slots too.
 template <class Src>
 __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src, uint32_t* bits, float* anc_s,
-                                           Shared& s) {
+                                           SharedA& s) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint8_t* bits8 = reinterpret_cast<const uint8_t*>(bits);
     Row R;
@@ -1290,20 +1294,9 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
                                            Buckets* bk, Shared& s) {
     const int tid = threadIdx.x, lane = tid & 31;
     const uint8_t* bits8 = reinterpret_cast<const uint8_t*>(bits);
+    // every global load of the row - parameters, ring state and kernel A's
+    // summary - issued together (a greedy row's summary loads go unused)
     const quasar_sample_params pr = a.d_params ? a.d_params[row] : a.h_params;
-    const bool shard = a.shard_cand != nullptr;  // a vocab shard: emit candidates, no draw
-    uint64_t* cand = shard ? a.shard_cand + (int64_t)row * a.shard_k : nullptr;
-    if (!(pr.temperature > 0.0f)) {
-        // greedy: finished by kernel A; a shard contributes its best column
-        if (shard && tid == 0) {
-            const quasar_shard_stat st = a.all_stats[(int64_t)a.shard_rank * a.B + row];
-            cand[0] = st.best >= 0 ? ((uint64_t)ord_key(st.max) << 32) | (uint32_t)(~(uint32_t)(a.col0 + st.best))
-                                   : 0ull;
-            for (int i = 1; i < a.shard_k; i++) cand[i] = 0ull;
-        }
-        return;
-    }
-    // every global load of the row summary, issued together
     Row R;
     const RowCtx c = row_ctx(a, row, pr, R);
     const RowParams& P = c.P;
@@ -1323,7 +1316,18 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
     const int2* pen = a.work_pen + (int64_t)row * a.hist_cap;
     const int2 pen0 = tid < a.hist_cap ? pen[tid] : make_int2(0, 0);  // used only if tid < npen
     uint64_t st_rng = a.rng ? a.rng[row] : 0ull;
-
+    const bool shard = a.shard_cand != nullptr;  // a vocab shard: emit candidates, no draw
+    uint64_t* cand = shard ? a.shard_cand + (int64_t)row * a.shard_k : nullptr;
+    if (!(pr.temperature > 0.0f)) {
+        // greedy: finished by kernel A; a shard contributes its best column
+        if (shard && tid == 0) {
+            const quasar_shard_stat st = a.all_stats[(int64_t)a.shard_rank * a.B + row];
+            cand[0] = st.best >= 0 ? ((uint64_t)ord_key(st.max) << 32) | (uint32_t)(~(uint32_t)(a.col0 + st.best))
+                                   : 0ull;
+            for (int i = 1; i < a.shard_k; i++) cand[i] = 0ull;
+        }
+        return;
+    }
     R.M = info.x;
     R.inv = info.y;
     if (shard) shard_norm(a, row, R.M, R.inv);  // the row's global max and 1/sum
@@ -1334,12 +1338,11 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
     s.tfmax[tid] = m;
     if (tid == 0) s.ncand = 0;
     // bitset of the penalized ids: re-reads leave them out, the select path
-    // penalizes them
+    // penalizes them (both come after barriers below)
     for (int i = tid; i < npen; i += CONSUMERS) {
         const int id = (i == tid ? pen0 : pen[i]).x;
         if (id >= 0 && id < R.V) atomicOr(&bits[id >> 5], 1u << (id & 31));
     }
-    csync();
 
     const double u = rng_unit(&st_rng);  // sample.c:173: one step per stochastic row
     int path = QUASAR_PATH_SELECT;
@@ -1349,8 +1352,12 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
     // (a shard emits k candidates per row: its rows need 1 <= top_k <= k)
     if (!(a.flags & QUASAR_FLAG_EXACT_SELECT) && (by_minp || by_topk) && (!shard || (by_topk && P.top_k <= a.shard_k))) {
         float tau = -INFINITY;
-        if (by_minp) tau = __fadd_rn(R.M, (float)(log((double)fminf(P.min_p, 1.0f)) - 0.01));
-        if (by_topk) tau = fmaxf(tau, topk_floor(P.top_k, s));
+        // (logf is within a few ulp: far inside the 0.01 margin)
+        if (by_minp) tau = __fadd_rn(R.M, logf(fminf(P.min_p, 1.0f)) - 0.01f);
+        if (by_topk) {
+            csync();  // every thread's max is in s.tfmax
+            tau = fmaxf(tau, topk_floor(P.top_k, s));
+        }
         const float lo = fmaxf(tau, R.thr);
         // qualifying thread-slots -> a shared list (bottom of buf), so the
         // re-reads spread over all threads; positions from a block scan
@@ -1524,25 +1531,16 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
         // merge reports id -1 for it)
         if (!done)
             for (int i = tid; i < a.shard_k; i += CONSUMERS) cand[i] = 0ull;
-        for (int i = tid; i < npen; i += CONSUMERS) {
-            const int id = (i == tid ? pen0 : pen[i]).x;
-            if (id >= 0 && id < R.V) bits[id >> 5] = 0u;
-        }
-        csync();
         return;
     }
     if (!done) {
         csync();
         select_path(R, bits8, reinterpret_cast<Hist*>(buf), P, u, s);
     }
-    const int chosen = *reinterpret_cast<volatile int*>(&s.abort) ? -1 : s.res_id;
-    for (int i = tid; i < npen; i += CONSUMERS) {
-        const int id = (i == tid ? pen0 : pen[i]).x;
-        if (id >= 0 && id < R.V) bits[id >> 5] = 0u;
+    if (tid == 0) {
+        const int chosen = *reinterpret_cast<volatile int*>(&s.abort) ? -1 : s.res_id;
+        write_row(a, row, c, chosen, s.res_nc, s.res_p, R.inv, path, st_rng);
     }
-    csync();
-    if (tid == 0) write_row(a, row, c, chosen, s.res_nc, s.res_p, R.inv, path, st_rng);
-    csync();
 }
 
 // ---------------------------------------------------------------------------
@@ -1553,7 +1551,7 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
 __global__ void __launch_bounds__(CONSUMERS, QS_A_CTAS) sample_rows_ldg(RowsArgs a) {
     extern __shared__ __align__(128) unsigned char dyn[];
     uint32_t* bits = reinterpret_cast<uint32_t*>(dyn);
-    __shared__ Shared s;
+    __shared__ SharedA s;
     __shared__ float anc_s[NCK * CONSUMERS];
     for (int i = threadIdx.x; i < a.nwords; i += CONSUMERS) bits[i] = 0u;
     if (threadIdx.x == 0) s.abort = 0;
@@ -1568,7 +1566,7 @@ __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a)
     float* ring = reinterpret_cast<float*>(dyn);
     uint32_t* bits = reinterpret_cast<uint32_t*>(dyn + NSTAGE * TILE_BYTES);
     uint64_t* bars = reinterpret_cast<uint64_t*>(dyn + NSTAGE * TILE_BYTES + ((a.nwords * 4 + 7) & ~7));
-    __shared__ Shared s;
+    __shared__ SharedA s;
     __shared__ float anc_s[NCK * CONSUMERS];
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + NSTAGE);
     if (threadIdx.x == 0) {
@@ -1635,7 +1633,7 @@ __global__ void __launch_bounds__(CONSUMERS, 3) sample_rows_finish(RowsArgs a) {
     for (int i = threadIdx.x; i < a.nwords; i += CONSUMERS) bits[i] = 0u;
     if (threadIdx.x == 0) s.abort = *reinterpret_cast<volatile int*>(a.work_abort);
     csync();
-    for (int row = blockIdx.x; row < a.B; row += gridDim.x) finish_row(a, row, buf, bits, bk, s);
+    if ((int)blockIdx.x < a.B) finish_row(a, blockIdx.x, buf, bits, bk, s);  // one row per CTA
 }
 
 // Merge of the vocab shards' candidates, one CTA per row: the G*k gathered
