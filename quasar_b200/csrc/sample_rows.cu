@@ -158,6 +158,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
         if (clock64() - t0 > WAIT_CYCLES) return false;
     return true;
 }
+__device__ __forceinline__ void lds4(uint32_t addr, float* v) {
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3])
+                 : "r"(addr)
+                 : "memory");
+}
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
@@ -171,6 +177,11 @@ __device__ __forceinline__ unsigned long long fixp(uint32_t pkey) {
 }
 
 // 256-bit streaming load of 8 floats (32-byte aligned address).
+__device__ __forceinline__ void ld4(const float* p, float* v) {
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3])
+                 : "l"(p));
+}
 __device__ __forceinline__ void ld8(const float* p, float* v) {
     asm volatile("ld.global.nc.L1::no_allocate.L2::evict_first.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                  : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]),
@@ -763,9 +774,23 @@ __device__ const uint64_t* bucket_sort_keys(uint64_t* buf, int nk, const Row& R,
 }
 
 // ---------------------------------------------------------------------------
-// Tile sources: where the consumers' 16 elements per tile come from. The
-// element -> thread mapping is the same for both: octets it*OCT_TILE + tid and
-// it*OCT_TILE + 256 + tid (index order within a thread is kept).
+// Tile sources: where the consumers' 16 elements per tile come from. Thread
+// tid owns the 16 contiguous elements 16*tid .. 16*tid+15 of each tile
+// (octets it*OCT_TILE + 2*tid and + 1), so a slot of kernel B's re-read is
+// one 64-byte span. In registers its four 4-element chunks sit in XOR order:
+// register chunk k holds chunk k ^ chunk_swz(tid). In the ring that makes the
+// 128-bit shared loads of eight neighbouring threads hit eight different
+// 16-byte bank groups; max and sum do not care about the order, and kernel
+// A's penalty bitset stores each id at pen_bit(id), the same permutation, so a
+// thread's 16 bits come out in register order.
+__device__ __forceinline__ int chunk_swz(int tid) { return (tid >> 1) & 3; }
+// Bit of id in kernel A's penalty bitset: chunk bits 2-3 flipped by the owner
+// thread's chunk_swz (bits 5-6 of id). Same 32-bit word as id.
+__device__ __forceinline__ int pen_bit(int id) { return id ^ (((id >> 5) & 3) << 2); }
+// Element index of register j of thread tid in tile it.
+__device__ __forceinline__ int reg_elem(int it, int tid, int j) {
+    return it * TILE_ELEMS + 16 * tid + 4 * ((j >> 2) ^ chunk_swz(tid)) + (j & 3);
+}
 
 struct LdgSource {
     static constexpr bool kRegs = true;
@@ -776,13 +801,17 @@ struct LdgSource {
             if (d < R.ntiles) load(R, d, nxt[d]);
     }
     __device__ __forceinline__ static void load(const Row& R, int it, float* v) {
-        const int o0 = it * OCT_TILE + threadIdx.x;
+        const int tid = threadIdx.x, sw = chunk_swz(tid);
+        const float* p = R.ptr + (int64_t)it * TILE_ELEMS + 16 * tid;
         if (R.vec && it + 1 < R.ntiles) {  // a full tile of a 32-byte aligned row
-            ld8(R.ptr + 8 * o0, v);
-            ld8(R.ptr + 8 * (o0 + CONSUMERS), v + 8);
+#pragma unroll
+            for (int k = 0; k < 4; k++) ld4(p + 4 * (k ^ sw), v + 4 * k);
         } else {
-            load_oct(R.ptr, o0, R.V, R.vec, v);
-            load_oct(R.ptr, o0 + CONSUMERS, R.V, R.vec, v + 8);
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const int e = reg_elem(it, tid, j);
+                v[j] = e < R.V ? __ldcs(R.ptr + e) : -INFINITY;
+            }
         }
     }
     // tile `it` into v; the loads of tile it+LDG_DEPTH are issued before returning
@@ -809,7 +838,8 @@ __device__ __noinline__ bool ring_wait_slow(uint32_t bar, uint32_t par, int* abo
 
 struct TmaSource {
     static constexpr bool kRegs = false;
-    const float* ring;  // NSTAGE tiles
+    uint32_t ring_u32;  // NSTAGE tiles (shared-window address)
+    uint32_t thr_off;   // 64 * tid + 16 * chunk_swz(tid)
     uint32_t full0, empty0;
     uint32_t g;  // chunks consumed by this CTA so far
     __device__ __forceinline__ void begin(const Row&) {}
@@ -823,23 +853,17 @@ struct TmaSource {
         // has not landed consults the abort flag
         const bool ok = mbar_try_wait(full0 + 8u * st, par) || ring_wait_slow(full0 + 8u * st, par, &s.abort);
         const int tid = threadIdx.x;
-        const float* t = ring + st * TILE_ELEMS;
-        const int e0 = it * TILE_ELEMS + 8 * tid, e1 = e0 + 8 * CONSUMERS;
         if (ok) {
-            const float4* p0 = reinterpret_cast<const float4*>(t + 8 * tid);
-            const float4* p1 = reinterpret_cast<const float4*>(t + 8 * (tid + CONSUMERS));
-            const float4 a = p0[0], b = p0[1], c = p1[0], d = p1[1];
-            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-            v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-            v[8] = c.x; v[9] = c.y; v[10] = c.z; v[11] = c.w;
-            v[12] = d.x; v[13] = d.y; v[14] = d.z; v[15] = d.w;
+            // chunk k ^ sw of the thread's 64 bytes: the address's bits 4-5
+            // start at sw (thr_off) and are flipped by k
+            const uint32_t base = ring_u32 + (uint32_t)st * TILE_BYTES + thr_off;
+#pragma unroll
+            for (int k = 0; k < 4; k++) lds4(base ^ (16u * k), v + 4 * k);
         }
         if (!ok || (kMaybeLast && it == R.ntiles - 1)) {  // only the last chunk of a row is partial
 #pragma unroll
-            for (int k = 0; k < 8; k++) {
-                if (!ok || e0 + k >= R.V) v[k] = -INFINITY;
-                if (!ok || e1 + k >= R.V) v[8 + k] = -INFINITY;
-            }
+            for (int j = 0; j < 16; j++)
+                if (!ok || reg_elem(it, tid, j) >= R.V) v[j] = -INFINITY;
         }
     }
     __device__ __forceinline__ void release() {
@@ -898,7 +922,7 @@ __device__ __forceinline__ RowCtx row_setup(const RowsArgs& a, int row, Row& R, 
     if (R.use_pen) {
         for (int i = threadIdx.x; i < c.len; i += CONSUMERS) {
             const int id = ring_id(c, i);
-            if (id >= 0 && id < a.V) atomicOr(&bits[id >> 5], 1u << (id & 31));
+            if (id >= 0 && id < a.V) atomicOr(&bits[id >> 5], 1u << (pen_bit(id) & 31));
         }
     }
     if (threadIdx.x == 0) s.npen = 0;
@@ -985,11 +1009,12 @@ __device__ __forceinline__ void stream_tiles(const Row& R, Src& src, Shared& s, 
 // x, x + -inf = -inf for finite x), with no per-element branch; warps with no
 // penalized element in the tile skip it.
 __device__ __forceinline__ void mask_penalized(const Row& R, const uint8_t* bits8, const float4* lut, float* v,
-                                               int o0, int o1) {
-    const uint32_t m0 = o0 < R.noct ? bits8[o0] : 0u;
-    const uint32_t m1 = o1 < R.noct ? bits8[o1] : 0u;
-    if (__any_sync(FULL, (m0 | m1) != 0u)) {
-        const float4 q[4] = {lut[m0 & 15u], lut[m0 >> 4], lut[m1 & 15u], lut[m1 >> 4]};
+                                               int it) {
+    // the thread's 16 bits (pen_bit order = register order), one 16-bit load
+    const int o0 = it * OCT_TILE + 2 * (int)threadIdx.x;
+    const uint32_t m = o0 < R.noct ? *reinterpret_cast<const uint16_t*>(bits8 + o0) : 0u;
+    if (__any_sync(FULL, m != 0u)) {
+        const float4 q[4] = {lut[m & 15u], lut[(m >> 4) & 15u], lut[(m >> 8) & 15u], lut[m >> 12]};
 #pragma unroll
         for (int k = 0; k < 4; k++) {
             const f32x2 lo = add2(pack2(v[4 * k], v[4 * k + 1]), pack2(q[k].x, q[k].y));
@@ -1031,7 +1056,7 @@ __device__ __forceinline__ void claim_penalized(const RowCtx& c, const Row& R, u
     for (int i = threadIdx.x; i < c.len; i += CONSUMERS) {
         const int id = ring_id(c, i);
         if (id >= 0 && id < R.V) {
-            const uint32_t bit = 1u << (id & 31);
+            const uint32_t bit = 1u << (pen_bit(id) & 31);
             if (atomicAnd(&bits[id >> 5], ~bit) & bit) f(id, penalize(__ldg(R.ptr + id), R.rp));
         }
     }
@@ -1066,17 +1091,18 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
         for (int it = 0; it < R.ntiles; it++) {
             float v[16];
             src.get(R, it, v, s);
-            const int o0 = it * OCT_TILE + tid, o1 = o0 + CONSUMERS;
-            if (R.use_pen) mask_penalized(R, bits8, s.pen_lut, v, o0, o1);
+            if (R.use_pen) mask_penalized(R, bits8, s.pen_lut, v, it);
             src.release();
             float mt = v[0];
 #pragma unroll
             for (int j = 1; j < 16; j++) mt = fmaxf(mt, v[j]);
             if (mt > bv) {  // strictly larger: the first index holding mt wins
-                int j = 0;
-                while (j < 15 && !(v[j] == mt)) j++;
+                int e = 0x7FFFFFFF;  // registers are not in index order
+#pragma unroll
+                for (int j = 0; j < 16; j++)
+                    if (v[j] == mt) e = min(e, reg_elem(it, tid, j));
                 bv = mt;
-                bi = j < 8 ? 8 * o0 + j : 8 * o1 + (j - 8);
+                bi = e;
             }
         }
         if (R.use_pen) {
@@ -1148,8 +1174,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
         constexpr bool kG1 = decltype(g1)::value;
         auto body = [&](float (&v)[16], int it, auto last) {
             constexpr bool kMaybeLast = decltype(last)::value;
-            if (R.use_pen)
-                mask_penalized(R, bits8, s.pen_lut, v, it * OCT_TILE + tid, it * OCT_TILE + tid + CONSUMERS);
+            if (R.use_pen) mask_penalized(R, bits8, s.pen_lut, v, it);
             // sample.c:142: sc = l * inv_t, rounded exactly like the reference
             // (packed pairs: each lane is the same IEEE multiply)
             f32x2 sc2[8];
@@ -1436,8 +1461,8 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
                     const uint32_t entry = i < nq ? qlist[i] : 0u;
                     const int sl = (int)(entry / CONSUMERS), owner = (int)(entry % CONSUMERS);
                     const int it = sl * g + t;
-                    o0[h] = it * OCT_TILE + owner;
-                    o1[h] = o0[h] + CONSUMERS;
+                    o0[h] = it * OCT_TILE + 2 * owner;  // the slot's 64 contiguous bytes
+                    o1[h] = o0[h] + 1;
                     if (i < nq && it < R.ntiles) {
                         load_oct_keep(R.ptr, o0[h], R.V, R.vec, sc[h]);
                         load_oct_keep(R.ptr, o1[h], R.V, R.vec, sc[h] + 8);
@@ -1545,7 +1570,7 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
 
 // ---------------------------------------------------------------------------
 // Kernels. Dynamic shared memory: kernel A row-load variant [bits]; kernel A
-// ring variant [ring NSTAGE x 16 KB][bits][full bars][empty bars]; kernel B
+// ring variant [to 64 B][ring NSTAGE x 16 KB][bits][full bars][empty bars]; kernel B
 // [scratch: candidate keys / select histograms][bits][counting-sort buckets].
 
 __global__ void __launch_bounds__(CONSUMERS, QS_A_CTAS) sample_rows_ldg(RowsArgs a) {
@@ -1563,9 +1588,12 @@ __global__ void __launch_bounds__(CONSUMERS, QS_A_CTAS) sample_rows_ldg(RowsArgs
 
 __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a) {
     extern __shared__ __align__(128) unsigned char dyn[];
-    float* ring = reinterpret_cast<float*>(dyn);
-    uint32_t* bits = reinterpret_cast<uint32_t*>(dyn + NSTAGE * TILE_BYTES);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(dyn + NSTAGE * TILE_BYTES + ((a.nwords * 4 + 7) & ~7));
+    // the ring starts on a 64-byte boundary (the chunk swizzle flips address
+    // bits 4-5 inside each thread's 64 bytes)
+    unsigned char* dyn64 = dyn + ((64u - (smem_u32(dyn) & 63u)) & 63u);
+    float* ring = reinterpret_cast<float*>(dyn64);
+    uint32_t* bits = reinterpret_cast<uint32_t*>(dyn64 + NSTAGE * TILE_BYTES);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(dyn64 + NSTAGE * TILE_BYTES + ((a.nwords * 4 + 7) & ~7));
     __shared__ SharedA s;
     __shared__ float anc_s[NCK * CONSUMERS];
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + NSTAGE);
@@ -1607,7 +1635,8 @@ __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a)
         return;
     }
     TmaSource src;
-    src.ring = ring;
+    src.ring_u32 = smem_u32(ring);
+    src.thr_off = 64u * threadIdx.x + 16u * chunk_swz(threadIdx.x);
     src.full0 = full0;
     src.empty0 = empty0;
     src.g = 0;
@@ -1692,8 +1721,8 @@ size_t rows_smem_bytes(int V) {  // kernel A, row-load variant
     return (size_t)nwords_for(V) * sizeof(uint32_t);
 }
 
-size_t rows_tma_smem_bytes(int V) {  // kernel A, ring variant
-    return (size_t)rows::NSTAGE * rows::TILE_BYTES + (((size_t)nwords_for(V) * 4 + 7) & ~(size_t)7) +
+size_t rows_tma_smem_bytes(int V) {  // kernel A, ring variant (+64: ring alignment)
+    return 64 + (size_t)rows::NSTAGE * rows::TILE_BYTES + (((size_t)nwords_for(V) * 4 + 7) & ~(size_t)7) +
            2 * rows::NSTAGE * sizeof(uint64_t);
 }
 
