@@ -66,6 +66,7 @@ constexpr int TOPK_MAX = CONSUMERS;            // largest top_k the candidate pa
 constexpr int QMAX = 4096;                     // qualifying thread-tiles re-read per row
 constexpr int NB = 1024;                       // radix bins per level (10 bits)
 constexpr long long WAIT_CYCLES = 1ll << 32;   // ~2 s: bound on any mbarrier wait
+constexpr float REF_SLACK = 64.0f;             // kernel A: exp reference lag (nats), e^64 << FLT_MAX
 #ifndef QS_LDG_DEPTH
 #define QS_LDG_DEPTH 1
 #endif
@@ -1163,9 +1164,13 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
     uint32_t tword = 0u;  // four slot bytes of this thread, stored together (tbl_off layout)
     float slotmax = -INFINITY;
     const f32x2 inv_t2 = pack2(R.inv_t, R.inv_t);
-    // the running max starts finite, so every term is exp(sc - m) with x <= 0
-    // from the first tile on (an all -inf stretch adds exp(-inf) = 0)
-    float m = -FLT_MAX;
+    // m: the thread's running max (tile table, anchors, kernel B). S sums
+    // exp(sc - m_ref) against a reference that moves only when a tile max
+    // passes it by more than REF_SLACK nats, so the double-precision rescale
+    // runs about once per row instead of at every new max; terms stay below
+    // e^REF_SLACK, far inside fp32 range. Both start finite (an all -inf
+    // stretch adds exp(-inf) = 0).
+    float m = -FLT_MAX, m_ref = -FLT_MAX;
     double S = 0.0;
     int next_ck = 0, ck = 0;  // next checkpoint slot (0, 1, 3, 7, 15, 31) and its index
     // g1: one tile per table slot (compile-time); last: std::true_type when
@@ -1187,14 +1192,15 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
             const float mt = fmaxf(max3(max3(sc[0], sc[1], sc[2]), max3(sc[3], sc[4], sc[5]),
                                         max3(sc[6], sc[7], sc[8])),
                                    max3(max3(sc[9], sc[10], sc[11]), max3(sc[12], sc[13], sc[14]), sc[15]));
-            if (mt > m) {
-                S *= exp((double)m - (double)mt);
-                m = mt;
+            m = fmaxf(m, mt);
+            if (mt > m_ref + REF_SLACK) {
+                S *= exp((double)m_ref - (double)mt);
+                m_ref = mt;
             }
             {
-                // sample.c:148 against the running max: x = sc - m, then the term
+                // sample.c:148 against the reference: x = sc - m_ref, then the term
                 f32x2 e[8];
-                const f32x2 nm2 = pack2(-m, -m);
+                const f32x2 nm2 = pack2(-m_ref, -m_ref);
 #pragma unroll
                 for (int j = 0; j < 8; j++) {
 #if QS_SUM_EXP == 3
@@ -1208,8 +1214,8 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
                         e[j] = exp_poly2(x0, x1);
                     }
 #else
-                    e[j] = pack2(sum_term_exp(__fsub_rn(sc[2 * j], m)),
-                                 sum_term_exp(__fsub_rn(sc[2 * j + 1], m)));
+                    e[j] = pack2(sum_term_exp(__fsub_rn(sc[2 * j], m_ref)),
+                                 sum_term_exp(__fsub_rn(sc[2 * j + 1], m_ref)));
 #endif
                 }
 #pragma unroll
@@ -1259,11 +1265,12 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
         claim_penalized(c, R, bits, [&](int id, float l) {
             const float sc = __fmul_rn(l, R.inv_t);
             pen[atomicAdd(&s.npen, 1)] = make_int2(id, __float_as_int(sc));
-            if (sc > m) {
-                S = (m > -INFINITY ? S * exp((double)m - (double)sc) : 0.0) + 1.0;
-                m = sc;
+            m = fmaxf(m, sc);
+            if (sc > m_ref + REF_SLACK) {
+                S = S * exp((double)m_ref - (double)sc) + 1.0;
+                m_ref = sc;
             } else if (sc > -INFINITY) {
-                S += exp((double)sc - (double)m);
+                S += exp((double)sc - (double)m_ref);
             }
         });
     }
@@ -1276,7 +1283,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
             if ((1 << k) - 1 < nsl) anc[tbl_off(k, tid)] = tile_deficit(m, anc_s[k * CONSUMERS + tid]);
     }
     const float M = block_max_f(m, s);
-    const double contrib = (m > -INFINITY) ? S * exp((double)m - (double)M) : 0.0;
+    const double contrib = S > 0.0 ? S * exp((double)m_ref - (double)M) : 0.0;
     const double Stot = block_sum_d(contrib, s);
     if (tid == 0) {
         a.work_info[row] = make_float4(M, __double2float_rn(1.0 / Stot), __int_as_float(s.npen), 0.0f);
