@@ -60,8 +60,16 @@ constexpr int TMAX_BYTES = TMAX_TILES * CONSUMERS;  // one byte per slot
 // coalesced load per four slots.
 __host__ __device__ constexpr int tbl_off(int slot, int tid) { return ((slot >> 2) * 256 + tid) * 4 + (slot & 3); }
 static_assert(TMAX_TILES % 4 == 0 && CONSUMERS == 256, "byte-table layout");
-constexpr int NCK = 6;                         // running-max checkpoints per thread: slots 0,1,3,7,15,31
+constexpr int NCK = 6;                         // running-max checkpoints per thread (slots: ck_slot)
 constexpr int ANC_BYTES = (NCK + 3) / 4 * 4 * CONSUMERS;  // checkpoint table per row (tbl_off layout)
+// Slot of checkpoint k: 1, 3, 7, 11, 19, 27. Slot j is bounded through the
+// first checkpoint at or after it (slots past 27: the thread's final max);
+// of the six-checkpoint sets whose later checkpoints close a 4-slot table
+// word, this one leaves kernel B the fewest slots to re-read on N(0, s)
+// rows (11 % fewer than 0, 1, 3, 7, 15, 31).
+__host__ __device__ constexpr int ck_slot(int k) {
+    return k == 0 ? 1 : k == 1 ? 3 : k == 2 ? 7 : k == 3 ? 11 : k == 4 ? 19 : 27;
+}
 constexpr int TOPK_MAX = CONSUMERS;            // largest top_k the candidate path takes
 constexpr int QMAX = 4096;                     // qualifying thread-tiles re-read per row
 constexpr int NB = 1024;                       // radix bins per level (10 bits)
@@ -1071,8 +1079,8 @@ __device__ __forceinline__ void claim_penalized(const RowCtx& c, const Row& R, u
 //
 // Tile-max table: one byte per thread and slot (a slot is g consecutive
 // tiles, g = 1 up to 40 tiles), the slot max's deficit below the thread's
-// running max m_j at the slot's end. The running max at slots 0,1,3,7,15,31
-// (checkpoints, kept in anc_s) is stored as a deficit below the thread's
+// running max m_j at the slot's end. The running max at the checkpoint slots
+// (ck_slot, kept in anc_s) is stored as a deficit below the thread's
 // final max, so slot j's max is bounded by final - (anchor deficit of the
 // first checkpoint >= j + slot deficit)/8: tight for early slots too.
 template <class Src>
@@ -1172,7 +1180,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
     // stretch adds exp(-inf) = 0).
     float m = -FLT_MAX, m_ref = -FLT_MAX;
     double S = 0.0;
-    int next_ck = 0, ck = 0;  // next checkpoint slot (0, 1, 3, 7, 15, 31) and its index
+    int next_ck = ck_slot(0), ck = 0;  // next checkpoint slot and its index
     // g1: one tile per table slot (compile-time); last: std::true_type when
     // `it` may be the row's last tile
     auto run = [&](auto g1) {
@@ -1232,9 +1240,9 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
                     tmax32[(it >> 2) * CONSUMERS + tid] = tword;
                     tword = 0u;
                 }
-                if (it == next_ck) {  // checkpoints are tiles 0, 1, 3, 7, 15, 31
+                if (it == next_ck) {
                     anc_s[ck * CONSUMERS + tid] = m;
-                    next_ck = ++ck < NCK ? 2 * next_ck + 1 : -1;
+                    next_ck = ++ck < NCK ? ck_slot(ck) : -1;
                 }
             } else {
                 slotmax = fmaxf(slotmax, mt);
@@ -1247,7 +1255,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
                     }
                     if (sl == next_ck) {
                         anc_s[ck * CONSUMERS + tid] = m;
-                        next_ck = ++ck < NCK ? 2 * next_ck + 1 : -1;
+                        next_ck = ++ck < NCK ? ck_slot(ck) : -1;
                     }
                     slotmax = -INFINITY;
                 }
@@ -1280,7 +1288,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
         uint8_t* anc = a.work_anc + (int64_t)row * ANC_BYTES;
 #pragma unroll
         for (int k = 0; k < NCK; k++)
-            if ((1 << k) - 1 < nsl) anc[tbl_off(k, tid)] = tile_deficit(m, anc_s[k * CONSUMERS + tid]);
+            if (ck_slot(k) < nsl) anc[tbl_off(k, tid)] = tile_deficit(m, anc_s[k * CONSUMERS + tid]);
     }
     const float M = block_max_f(m, s);
     const double contrib = S > 0.0 ? S * exp((double)m_ref - (double)M) : 0.0;
@@ -1300,12 +1308,6 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
 // elements reach it). Only thread-slots whose bound clears the threshold are
 // read again; penalized ids come from kernel A's list. Rows it cannot bound
 // take the exact select path.
-
-// Checkpoint slot index whose anchor bounds slot sl: the first of
-// 0,1,3,7,15,31 at or after sl (NCK = none: the thread's final max).
-__host__ __device__ constexpr int ck_of(int sl) {
-    return sl == 0 ? 0 : sl == 1 ? 1 : sl <= 3 ? 2 : sl <= 7 ? 3 : sl <= 15 ? 4 : sl <= 31 ? 5 : NCK;
-}
 
 // Global max M and inv = (float)(1/sum) of a row split into vocab shards,
 // from the shards' (max, sum against that max) pairs - the same combination
@@ -1401,7 +1403,7 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
         uint32_t keep0 = 0u, keep1 = 0u;
 #pragma unroll
         for (int k = 0; k < NCK; k++)
-            if ((1 << k) - 1 < nsl) (k < 4 ? keep0 : keep1) |= 255u << (8 * (k & 3));
+            if (ck_slot(k) < nsl) (k < 4 ? keep0 : keep1) |= 255u << (8 * (k & 3));
         const uint32_t ea = ew[0] & keep0, eb = ew[1] & keep1;
         const float xd = __fmul_ru(__fsub_ru(m, lo), 8.0f);
         const int X = !(xd < 1000.0f) ? 1000 : (xd < -1.0f ? -1 : (int)floorf(xd) + 1);  // NaN -> 1000
@@ -1414,15 +1416,17 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
         for (int q = 0; q < DW; q++) {
             const uint32_t d4 = dw[q];
             uint32_t r;
-            if (q == 0) {  // slots 0, 1, 2-3: checkpoints 0, 1, 2
-                const int t0 = thr(ea & 255u), t1 = thr((ea >> 8) & 255u), t2 = thr((ea >> 16) & 255u);
+            if (q == 0) {  // slots 0-1: checkpoint 0 (slot 1); slots 2-3: checkpoint 1 (slot 3)
+                const int t0 = thr(ea & 255u), t1 = thr((ea >> 8) & 255u);
                 r = (t0 >= 0 && (d4 & 255u) <= (uint32_t)t0 ? 1u : 0u) |
-                    (t1 >= 0 && ((d4 >> 8) & 255u) <= (uint32_t)t1 ? 2u : 0u) |
-                    (t2 >= 0 && ((d4 >> 16) & 255u) <= (uint32_t)t2 ? 4u : 0u) |
-                    (t2 >= 0 && (d4 >> 24) <= (uint32_t)t2 ? 8u : 0u);
+                    (t0 >= 0 && ((d4 >> 8) & 255u) <= (uint32_t)t0 ? 2u : 0u) |
+                    (t1 >= 0 && ((d4 >> 16) & 255u) <= (uint32_t)t1 ? 4u : 0u) |
+                    (t1 >= 0 && (d4 >> 24) <= (uint32_t)t1 ? 8u : 0u);
             } else {
-                // checkpoint of slots 4q..4q+3: 3 (q=1), 4 (q<=3), 5 (q<=7), none
-                const uint32_t ek = q == 1 ? (ea >> 24) : q <= 3 ? (eb & 255u) : q <= 7 ? ((eb >> 8) & 255u) : 0u;
+                // checkpoint of slots 4q..4q+3: 2 (q=1, slot 7), 3 (q=2, slot 11),
+                // 4 (q<=4, slot 19), 5 (q<=6, slot 27), none (the final max)
+                const uint32_t ek = q == 1 ? ((ea >> 16) & 255u) : q == 2 ? (ea >> 24) : q <= 4 ? (eb & 255u)
+                                  : q <= 6 ? ((eb >> 8) & 255u) : 0u;
                 const int tq = thr(ek);
                 const uint32_t cmp = __vcmpleu4(d4, (uint32_t)max(tq, 0) * 0x01010101u);  // 0xFF per slot <= tq
                 r = tq < 0 ? 0u : (((cmp >> 7) & 1u) | ((cmp >> 14) & 2u) | ((cmp >> 21) & 4u) | ((cmp >> 28) & 8u));
