@@ -662,6 +662,81 @@ __device__ void candidate_cuts(const uint64_t* keys, int nk, const RowParams& P,
     csync();
 }
 
+// Cuts and draw for a short candidate list (nk <= RANK_MAX), without sorting
+// and with four barriers: thread t < nk takes raw entry t (at buf[CAP - nk,
+// CAP)), finds its rank in (p desc, id asc) order and the mass above it by
+// scanning all nk keys, so every cumsum of candidate_cuts is known at its
+// rank. Masses are exact integer sums of p * 2^54 (each p <= 1, nk <= 256:
+// no overflow), so the cumsums agree with the reference's double sums far
+// inside the CDF tolerance. A vocab shard (cand != nullptr) writes its first
+// shard_k keys in order instead, ids made global.
+constexpr int RANK_MAX = CONSUMERS;
+__device__ void rank_cuts(uint64_t* buf, int nk, const Row& R, const RowParams& P, float floor_p, double u,
+                          Shared& s, uint64_t* cand, int shard_k, int64_t col0) {
+    const int tid = threadIdx.x;
+    const int BEYOND = 0x7FFFFFFF;
+    ulonglong2* E = reinterpret_cast<ulonglong2*>(buf);  // {key, p * 2^54}, buf[0, 2 nk): below the raw entries
+    uint64_t key = 0ull;
+    float p = 0.0f;
+    unsigned long long fix = 0ull;
+    if (tid < nk) {
+        const uint64_t en = buf[CAP - nk + tid];
+        const uint32_t pk = p_key(__uint_as_float((uint32_t)(en >> 32)), R.M, R.thr, R.inv);
+        key = ((uint64_t)pk << 32) | (uint32_t)(~(uint32_t)en);
+        p = __uint_as_float(pk);
+        fix = __float2ull_rz(p * 18014398509481984.0f);  // p * 2^54, exact
+    }
+    if (tid == 0) {
+        s.cut_p = BEYOND;
+        s.cut_m = nk;
+        s.cut_d = BEYOND;
+    }
+    csync();  // every raw entry is read
+    if (tid < nk) E[tid] = make_ulonglong2(key, fix);
+    csync();
+    int rank = 0;
+    unsigned long long above = 0ull;
+    if (tid < nk) {
+#pragma unroll 4
+        for (int j = 0; j < nk; j++) {
+            const ulonglong2 e = E[j];
+            const bool gt = e.x > key;
+            rank += gt ? 1 : 0;
+            above += gt ? e.y : 0ull;
+        }
+    }
+    if (cand) {
+        if (tid < nk && rank < shard_k)
+            cand[rank] = (key & 0xFFFFFFFF00000000ull) | (uint32_t)(~(uint32_t)(col0 + (int64_t)(~(uint32_t)key)));
+        for (int i = nk + tid; i < shard_k; i += CONSUMERS) cand[i] = 0ull;
+        return;
+    }
+    const double cum = (double)(above + fix) * 0x1p-54;  // inclusive cumsum at this rank
+    const int nc1 = (P.top_k > 0 && P.top_k < nk) ? P.top_k : BEYOND;
+    if (tid < nk) {
+        // top-k (sample.c:154); top-p (sample.c:156-160): first prefix whose
+        // cumsum reaches top_p; min-p (sample.c:162-167): first i >= 1 below
+        // the floor (none: nk)
+        if (P.top_p < 1.0f && rank < min(nc1, nk) && cum >= (double)P.top_p) atomicMin(&s.cut_p, rank + 1);
+        if (rank >= 1 && p < floor_p) atomicMin(&s.cut_m, rank);
+    }
+    csync();
+    const int nc2 = s.cut_p != BEYOND ? s.cut_p : nc1;
+    const int nc = max(1, min(nc2, s.cut_m));
+    if (tid < nk && rank == nc - 1) s.rsum = cum;  // the kept mass (sample.c:171-172)
+    csync();
+    const double r = u * s.rsum;  // sample.c:173-175: first kept i with r <= cumsum
+    if (tid < nk && rank < nc && cum >= r) atomicMin(&s.cut_d, rank);
+    csync();
+    const int chosen = s.cut_d != BEYOND ? s.cut_d : nc - 1;
+    if (tid < nk && rank == chosen) {
+        s.res_id = (int)(~(uint32_t)key);
+        s.res_nc = nc;
+        s.res_p = p;
+    }
+    csync();
+}
+
 // Tile-max table entry: how far (in 1/8 nat, rounded down, saturating at 255)
 // a slot's max lies below the thread's running max m at the slot's end. Since
 // m only grows, slot max <= (thread's final max) - d/8 holds at the end.
@@ -1521,7 +1596,11 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
         }
         csync();
         const int nk = nq_all <= QMAX ? s.ncand : CAP + 1;
-        if (nk > 0 && nk <= room) {
+        if (nk > 0 && nk <= RANK_MAX) {
+            rank_cuts(buf, nk, R, P, by_minp ? __fmul_rn(P.min_p, R.inv) : 0.0f, u, s, cand, a.shard_k, a.col0);
+            done = true;
+            path = QUASAR_PATH_CANDIDATE;
+        } else if (nk > 0 && nk <= room) {
             const uint64_t* keys = buf;
             // raw entries live in buf[CAP - nk, CAP)
             // counting sort; a full bitonic sort for very large or clustered lists
