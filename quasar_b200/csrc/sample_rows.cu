@@ -1425,6 +1425,8 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
     const int2* pen = a.work_pen + (int64_t)row * a.hist_cap;
     const int2 pen0 = tid < a.hist_cap ? pen[tid] : make_int2(0, 0);  // used only if tid < npen
     uint64_t st_rng = a.rng ? a.rng[row] : 0ull;
+    // kernel A's abort word (read where the row is written)
+    const int aborted = tid == 0 ? *reinterpret_cast<volatile int*>(a.work_abort) : 0;
     const bool shard = a.shard_cand != nullptr;  // a vocab shard: emit candidates, no draw
     uint64_t* cand = shard ? a.shard_cand + (int64_t)row * a.shard_k : nullptr;
     if (!(pr.temperature > 0.0f)) {
@@ -1437,6 +1439,9 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
         }
         return;
     }
+    // the bitset starts empty (shared memory is not cleared between CTAs);
+    // the loads above are in flight meanwhile
+    for (int i = tid; i < a.nwords; i += CONSUMERS) bits[i] = 0u;
     R.M = info.x;
     R.inv = info.y;
     if (shard) shard_norm(a, row, R.M, R.inv);  // the row's global max and 1/sum
@@ -1446,6 +1451,7 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
     R.use_pen = npen > 0;
     s.tfmax[tid] = m;
     if (tid == 0) s.ncand = 0;
+    csync();  // the bitset is clear
     // bitset of the penalized ids: re-reads leave them out, the select path
     // penalizes them (both come after barriers below)
     for (int i = tid; i < npen; i += CONSUMERS) {
@@ -1566,10 +1572,11 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
 #pragma unroll
                         for (int j = 0; j < 16; j++) {
                             sc[h][j] = __fmul_rn(sc[h][j], R.inv_t);
-                            const int idx = j < 8 ? 8 * o0[h] + j : 8 * o1[h] + (j - 8);
-                            mk |= (sc[h][j] >= lo && idx < R.V ? 1u : 0u) << j;
+                            mk |= (sc[h][j] >= lo ? 1u : 0u) << j;
                         }
-                        mask[h] = mk;
+                        // elements 8*o0 + j (contiguous); only the row's last slot is partial
+                        const int left = R.V - 8 * o0[h];
+                        mask[h] = left >= 16 ? mk : mk & ((1u << max(left, 0)) - 1u);
                     }
                     cnt2 += __popc(mask[h]);
                 }
@@ -1580,14 +1587,19 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
                 pos = __shfl_sync(FULL, pos, 31) + incl2 - cnt2;
 #pragma unroll
                 for (int h = 0; h < 2; h++) {
-                    if (mask[h]) {
+                    const uint32_t mh = mask[h];
 #pragma unroll
-                        for (int j = 0; j < 16; j++) {
-                            if (mask[h] & (1u << j)) {
-                                const int idx = j < 8 ? 8 * o0[h] + j : 8 * o1[h] + (j - 8);
-                                if (pos < room)
-                                    buf[CAP - 1 - pos] = ((uint64_t)__float_as_uint(sc[h][j]) << 32) | (uint32_t)idx;
-                                pos++;
+                    for (int nb = 0; nb < 4; nb++) {
+                        if (mh & (15u << (4 * nb))) {  // most survivors come one or two per slot
+#pragma unroll
+                            for (int k = 0; k < 4; k++) {
+                                const int j = 4 * nb + k;
+                                if (mh & (1u << j)) {
+                                    if (pos < room)
+                                        buf[CAP - 1 - pos] =
+                                            ((uint64_t)__float_as_uint(sc[h][j]) << 32) | (uint32_t)(8 * o0[h] + j);
+                                    pos++;
+                                }
                             }
                         }
                     }
@@ -1652,10 +1664,7 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
         csync();
         select_path(R, bits8, reinterpret_cast<Hist*>(buf), P, u, s);
     }
-    if (tid == 0) {
-        const int chosen = *reinterpret_cast<volatile int*>(&s.abort) ? -1 : s.res_id;
-        write_row(a, row, c, chosen, s.res_nc, s.res_p, R.inv, path, st_rng);
-    }
+    if (tid == 0) write_row(a, row, c, aborted ? -1 : s.res_id, s.res_nc, s.res_p, R.inv, path, st_rng);
 }
 
 // ---------------------------------------------------------------------------
@@ -1749,9 +1758,6 @@ __global__ void __launch_bounds__(CONSUMERS, 3) sample_rows_finish(RowsArgs a) {
     uint32_t* bits = reinterpret_cast<uint32_t*>(dyn + FINISH_SCRATCH);
     Buckets* bk = reinterpret_cast<Buckets*>(dyn + FINISH_SCRATCH + (((size_t)a.nwords * 4 + 15) & ~(size_t)15));
     __shared__ Shared s;
-    for (int i = threadIdx.x; i < a.nwords; i += CONSUMERS) bits[i] = 0u;
-    if (threadIdx.x == 0) s.abort = *reinterpret_cast<volatile int*>(a.work_abort);
-    csync();
     if ((int)blockIdx.x < a.B) finish_row(a, blockIdx.x, buf, bits, bk, s);  // one row per CTA
 }
 
