@@ -179,6 +179,12 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
         "l"(src), "r"(bytes), "r"(bar)
         : "memory");
 }
+// Asynchronous 4-byte global -> shared copy (cp.async) and its wait.
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 // Mass fixed point: p * 2^62 truncated (p <= 1, row sums stay below 2^64).
 __device__ __forceinline__ unsigned long long fixp(uint32_t pkey) {
@@ -1001,13 +1007,25 @@ __device__ __forceinline__ RowCtx row_ctx(const RowsArgs& a, int row, const quas
 }
 
 // row_ctx plus the penalty bitset of the row's history ids (consumer threads).
-__device__ __forceinline__ RowCtx row_setup(const RowsArgs& a, int row, Row& R, uint32_t* bits, Shared& s) {
+// my_id: this thread's ring entry (threadIdx.x) when it is a column id, else
+// -1; its logit is copied into s.tfmax[threadIdx.x] (idle in kernel A) while
+// the row streams, for claim_penalized.
+__device__ __forceinline__ RowCtx row_setup(const RowsArgs& a, int row, Row& R, uint32_t* bits, Shared& s,
+                                            int& my_id) {
     const RowCtx c = row_ctx(a, row, a.d_params ? a.d_params[row] : a.h_params, R);
+    my_id = -1;
     if (R.use_pen) {
         for (int i = threadIdx.x; i < c.len; i += CONSUMERS) {
             const int id = ring_id(c, i);
-            if (id >= 0 && id < a.V) atomicOr(&bits[id >> 5], 1u << (pen_bit(id) & 31));
+            if (id >= 0 && id < a.V) {
+                atomicOr(&bits[id >> 5], 1u << (pen_bit(id) & 31));
+                if (i == (int)threadIdx.x) {
+                    my_id = id;
+                    cp_async4(smem_u32(&s.tfmax[threadIdx.x]), R.ptr + id);
+                }
+            }
         }
+        cp_async_commit();
     }
     if (threadIdx.x == 0) s.npen = 0;
     csync();
@@ -1135,13 +1153,19 @@ __device__ __forceinline__ void exclude_penalized(const Row& R, const uint8_t* b
 // logit) (sample.c:118-128) exactly once: the thread whose atomic clears the
 // id's bit owns it. Leaves the bitset all zero. Callers synchronise first so
 // that no thread still reads the bitset.
+// Entry threadIdx.x comes from row_setup (my_id, logit staged in s.tfmax);
+// entries past the first CONSUMERS are read here.
 template <class F>
-__device__ __forceinline__ void claim_penalized(const RowCtx& c, const Row& R, uint32_t* bits, F&& f) {
+__device__ __forceinline__ void claim_penalized(const RowCtx& c, const Row& R, uint32_t* bits, int my_id,
+                                                const Shared& s, F&& f) {
+    cp_async_wait_all();  // this thread's staged logit
     for (int i = threadIdx.x; i < c.len; i += CONSUMERS) {
-        const int id = ring_id(c, i);
+        const bool first = i == (int)threadIdx.x;
+        const int id = first ? my_id : ring_id(c, i);
         if (id >= 0 && id < R.V) {
             const uint32_t bit = 1u << (pen_bit(id) & 31);
-            if (atomicAnd(&bits[id >> 5], ~bit) & bit) f(id, penalize(__ldg(R.ptr + id), R.rp));
+            if (atomicAnd(&bits[id >> 5], ~bit) & bit)
+                f(id, penalize(first ? s.tfmax[threadIdx.x] : __ldg(R.ptr + id), R.rp));
         }
     }
 }
@@ -1164,7 +1188,8 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint8_t* bits8 = reinterpret_cast<const uint8_t*>(bits);
     Row R;
-    const RowCtx c = row_setup(a, row, R, bits, s);
+    int my_id;
+    const RowCtx c = row_setup(a, row, R, bits, s, my_id);
     const RowParams& P = c.P;
     src.begin(R);
 
@@ -1193,7 +1218,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
             csync();
             // penalized ids compete by (value desc, id asc); -inf never wins,
             // so an all -inf row still gives id 0 (sample.c:130-134)
-            claim_penalized(c, R, bits, [&](int id, float l) {
+            claim_penalized(c, R, bits, my_id, s, [&](int id, float l) {
                 if (l > bv || (l == bv && id < bi && l > -INFINITY)) {
                     bv = l;
                     bi = id;
@@ -1345,7 +1370,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
         // the penalized elements join the running max and sum exactly, and
         // are listed for kernel B
         int2* pen = a.work_pen + (int64_t)row * a.hist_cap;
-        claim_penalized(c, R, bits, [&](int id, float l) {
+        claim_penalized(c, R, bits, my_id, s, [&](int id, float l) {
             const float sc = __fmul_rn(l, R.inv_t);
             pen[atomicAdd(&s.npen, 1)] = make_int2(id, __float_as_int(sc));
             m = fmaxf(m, sc);
@@ -1353,7 +1378,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
                 S = S * exp((double)m_ref - (double)sc) + 1.0;
                 m_ref = sc;
             } else if (sc > -INFINITY) {
-                S += exp((double)sc - (double)m_ref);
+                S += (double)exp_fast(__fsub_rn(sc, m_ref));  // like the streamed terms
             }
         });
     }
