@@ -128,6 +128,10 @@ struct Shared {
 // Kernel A's shared state: the common slots plus the penalty mask table.
 struct SharedA : Shared {
     float4 pen_lut[16];   // nibble n -> +0 / -inf per bit (penalized elements leave the stream)
+    // the CTA's next row, copied during the current row's tail (stage_next_row):
+    // parameters and ring position; its first CONSUMERS ring slots go to tfmax
+    quasar_sample_params nxt_pr;
+    int nxt_len, nxt_head;
 };
 
 // Barrier of the 256 consumer threads (warps 0-7); the TMA producer warp never
@@ -981,7 +985,10 @@ __device__ __forceinline__ int ring_id(const RowCtx& c, int i) {
 }
 
 // Row parameters and history ring of `row` (no shared-memory work).
-__device__ __forceinline__ RowCtx row_ctx(const RowsArgs& a, int row, const quasar_sample_params& pr, Row& R) {
+// len_raw / head_raw: the row's hist_len / hist_head entries as stored (or
+// the defaults of ring_len_raw / ring_head_raw).
+__device__ __forceinline__ RowCtx row_ctx_raw(const RowsArgs& a, int row, const quasar_sample_params& pr,
+                                              int len_raw, int head_raw, Row& R) {
     RowCtx c;
     c.P = clamp_params(pr);
     c.cap = a.hist ? a.hist_cap : 0;
@@ -991,8 +998,8 @@ __device__ __forceinline__ RowCtx row_ctx(const RowsArgs& a, int row, const quas
     c.col0 = a.col0;
     if (c.cap > 0) {
         c.ring = a.hist + (int64_t)row * c.cap;
-        c.len = a.hist_len ? min(max(a.hist_len[row], 0), c.cap) : c.cap;
-        c.head = a.hist_head ? ((a.hist_head[row] % c.cap) + c.cap) % c.cap : 0;
+        c.len = min(max(len_raw, 0), c.cap);
+        c.head = ((head_raw % c.cap) + c.cap) % c.cap;
     }
     R.ptr = a.logits + (int64_t)row * a.ld;
     R.V = a.V;
@@ -1006,22 +1013,65 @@ __device__ __forceinline__ RowCtx row_ctx(const RowsArgs& a, int row, const quas
     return c;
 }
 
+__device__ __forceinline__ bool has_len(const RowsArgs& a) { return a.hist && a.hist_cap > 0 && a.hist_len; }
+__device__ __forceinline__ bool has_head(const RowsArgs& a) { return a.hist && a.hist_cap > 0 && a.hist_head; }
+__device__ __forceinline__ int ring_len_raw(const RowsArgs& a, int row) { return has_len(a) ? a.hist_len[row] : a.hist_cap; }
+__device__ __forceinline__ int ring_head_raw(const RowsArgs& a, int row) { return has_head(a) ? a.hist_head[row] : 0; }
+__device__ __forceinline__ RowCtx row_ctx(const RowsArgs& a, int row, const quasar_sample_params& pr, Row& R) {
+    return row_ctx_raw(a, row, pr, ring_len_raw(a, row), ring_head_raw(a, row), R);
+}
+
 // row_ctx plus the penalty bitset of the row's history ids (consumer threads).
 // my_id: this thread's ring entry (threadIdx.x) when it is a column id, else
 // -1; its logit is copied into s.tfmax[threadIdx.x] (idle in kernel A) while
 // the row streams, for claim_penalized.
-__device__ __forceinline__ RowCtx row_setup(const RowsArgs& a, int row, Row& R, uint32_t* bits, Shared& s,
-                                            int& my_id) {
-    const RowCtx c = row_ctx(a, row, a.d_params ? a.d_params[row] : a.h_params, R);
+// Ring slot p (a raw position) holds a history entry when it is one of the
+// len slots from head on.
+__device__ __forceinline__ bool ring_slot_used(const RowCtx& c, int p) {
+    return p - c.head + (p < c.head ? c.cap : 0) < c.len;
+}
+// Copies the inputs row_setup needs for `row` into shared memory (cp.async,
+// one group): parameters, ring length and head, ring slots 0..CONSUMERS-1
+// (raw positions, into tfmax). Rows past B are skipped.
+__device__ __forceinline__ void stage_next_row(const RowsArgs& a, int row, SharedA& s) {
+    const int tid = threadIdx.x;
+    if (row < a.B) {
+        if (a.d_params && tid < (int)(sizeof(quasar_sample_params) / 4))
+            cp_async4(smem_u32(&s.nxt_pr) + 4u * tid, reinterpret_cast<const char*>(a.d_params + row) + 4 * tid);
+        if (tid == 32 && has_len(a)) cp_async4(smem_u32(&s.nxt_len), a.hist_len + row);
+        if (tid == 64 && has_head(a)) cp_async4(smem_u32(&s.nxt_head), a.hist_head + row);
+        if (a.hist && tid < a.hist_cap)
+            cp_async4(smem_u32(&s.tfmax[tid]), a.hist + (int64_t)row * a.hist_cap + tid);
+    }
+    cp_async_commit();
+}
+// staged: stage_next_row ran for this row. my_id: the column id in this
+// thread's ring slot (threadIdx.x) when that slot holds an entry, else -1;
+// its logit is copied into s.tfmax[threadIdx.x] (idle in kernel A) while the
+// row streams, for claim_penalized.
+__device__ __forceinline__ RowCtx row_setup(const RowsArgs& a, int row, Row& R, uint32_t* bits, SharedA& s,
+                                            int& my_id, bool staged) {
+    const int tid = threadIdx.x;
+    if (staged) {
+        cp_async_wait_all();
+        csync();  // every thread's copies have landed
+    }
+    const quasar_sample_params pr = a.d_params ? (staged ? s.nxt_pr : a.d_params[row]) : a.h_params;
+    const int len_raw = staged ? (has_len(a) ? s.nxt_len : a.hist_cap) : ring_len_raw(a, row);
+    const int head_raw = staged ? (has_head(a) ? s.nxt_head : 0) : ring_head_raw(a, row);
+    const RowCtx c = row_ctx_raw(a, row, pr, len_raw, head_raw, R);
     my_id = -1;
     if (R.use_pen) {
-        for (int i = threadIdx.x; i < c.len; i += CONSUMERS) {
-            const int id = ring_id(c, i);
-            if (id >= 0 && id < a.V) {
+        for (int p = tid; p < c.cap; p += CONSUMERS) {
+            if (!ring_slot_used(c, p)) continue;
+            const int raw = (staged && p == tid) ? __float_as_int(s.tfmax[tid]) : c.ring[p];
+            const int64_t id64 = (int64_t)raw - c.col0;
+            const int id = (id64 >= 0 && id64 < a.V) ? (int)id64 : -1;
+            if (id >= 0) {
                 atomicOr(&bits[id >> 5], 1u << (pen_bit(id) & 31));
-                if (i == (int)threadIdx.x) {
+                if (p == tid) {
                     my_id = id;
-                    cp_async4(smem_u32(&s.tfmax[threadIdx.x]), R.ptr + id);
+                    cp_async4(smem_u32(&s.tfmax[tid]), R.ptr + id);
                 }
             }
         }
@@ -1153,15 +1203,20 @@ __device__ __forceinline__ void exclude_penalized(const Row& R, const uint8_t* b
 // logit) (sample.c:118-128) exactly once: the thread whose atomic clears the
 // id's bit owns it. Leaves the bitset all zero. Callers synchronise first so
 // that no thread still reads the bitset.
-// Entry threadIdx.x comes from row_setup (my_id, logit staged in s.tfmax);
-// entries past the first CONSUMERS are read here.
+// Ring slot threadIdx.x comes from row_setup (my_id, logit staged in
+// s.tfmax); slots past the first CONSUMERS are read here.
 template <class F>
 __device__ __forceinline__ void claim_penalized(const RowCtx& c, const Row& R, uint32_t* bits, int my_id,
                                                 const Shared& s, F&& f) {
     cp_async_wait_all();  // this thread's staged logit
-    for (int i = threadIdx.x; i < c.len; i += CONSUMERS) {
-        const bool first = i == (int)threadIdx.x;
-        const int id = first ? my_id : ring_id(c, i);
+    for (int p = threadIdx.x; p < c.cap; p += CONSUMERS) {
+        const bool first = p == (int)threadIdx.x;
+        int id = my_id;
+        if (!first) {
+            if (!ring_slot_used(c, p)) continue;
+            const int64_t id64 = (int64_t)c.ring[p] - c.col0;
+            id = (id64 >= 0 && id64 < R.V) ? (int)id64 : -1;
+        }
         if (id >= 0 && id < R.V) {
             const uint32_t bit = 1u << (pen_bit(id) & 31);
             if (atomicAnd(&bits[id >> 5], ~bit) & bit)
@@ -1184,12 +1239,12 @@ __device__ __forceinline__ void claim_penalized(const RowCtx& c, const Row& R, u
 // first checkpoint >= j + slot deficit)/8: tight for early slots too.
 template <class Src>
 __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src, uint32_t* bits, float* anc_s,
-                                           SharedA& s) {
+                                           SharedA& s, bool staged) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint8_t* bits8 = reinterpret_cast<const uint8_t*>(bits);
     Row R;
     int my_id;
-    const RowCtx c = row_setup(a, row, R, bits, s, my_id);
+    const RowCtx c = row_setup(a, row, R, bits, s, my_id, staged);
     const RowParams& P = c.P;
     src.begin(R);
 
@@ -1225,6 +1280,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
                 }
             });
         }
+        stage_next_row(a, row + (int)gridDim.x, s);  // s.tfmax is free again
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const float ov = __shfl_xor_sync(FULL, bv, o);
@@ -1382,6 +1438,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
             }
         });
     }
+    stage_next_row(a, row + (int)gridDim.x, s);  // s.tfmax is free again
     a.work_tfmax[(int64_t)row * CONSUMERS + tid] = m;
     {
         const int nsl = (R.ntiles + g - 1) / g;
@@ -1707,7 +1764,7 @@ __global__ void __launch_bounds__(CONSUMERS, QS_A_CTAS) sample_rows_ldg(RowsArgs
     init_pen_lut(s);
     csync();
     LdgSource src;
-    for (int row = blockIdx.x; row < a.B; row += gridDim.x) stream_row(a, row, src, bits, anc_s, s);
+    for (int row = blockIdx.x; row < a.B; row += gridDim.x) stream_row(a, row, src, bits, anc_s, s, row != (int)blockIdx.x);
 }
 
 __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a) {
@@ -1764,7 +1821,7 @@ __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a)
     src.full0 = full0;
     src.empty0 = empty0;
     src.g = 0;
-    for (int row = blockIdx.x; row < a.B; row += gridDim.x) stream_row(a, row, src, bits, anc_s, s);
+    for (int row = blockIdx.x; row < a.B; row += gridDim.x) stream_row(a, row, src, bits, anc_s, s, row != (int)blockIdx.x);
     // After an abort, give chunks still in flight a bounded chance to land
     // before the CTA (and its shared memory) goes away; the rows of this CTA
     // are marked failed (id -1) by kernel B through the abort word.
