@@ -1441,11 +1441,16 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
     stage_next_row(a, row + (int)gridDim.x, s);  // s.tfmax is free again
     a.work_tfmax[(int64_t)row * CONSUMERS + tid] = m;
     {
+        // anchor deficits, four per word (tbl_off), stored as whole words;
+        // checkpoints past the last slot stay 0 (kernel B ignores them)
         const int nsl = (R.ntiles + g - 1) / g;
-        uint8_t* anc = a.work_anc + (int64_t)row * ANC_BYTES;
+        uint32_t* anc = reinterpret_cast<uint32_t*>(a.work_anc + (int64_t)row * ANC_BYTES);
+        uint32_t w[(NCK + 3) / 4] = {};
 #pragma unroll
         for (int k = 0; k < NCK; k++)
-            if (ck_slot(k) < nsl) anc[tbl_off(k, tid)] = tile_deficit(m, anc_s[k * CONSUMERS + tid]);
+            if (ck_slot(k) < nsl) w[k >> 2] |= (uint32_t)tile_deficit(m, anc_s[k * CONSUMERS + tid]) << (8 * (k & 3));
+#pragma unroll
+        for (int q = 0; q < (NCK + 3) / 4; q++) anc[q * CONSUMERS + tid] = w[q];
     }
     const float M = block_max_f(m, s);
     const double contrib = S > 0.0 ? S * exp((double)m_ref - (double)M) : 0.0;
