@@ -1160,11 +1160,13 @@ __device__ __forceinline__ void stream_tiles(const Row& R, Src& src, Shared& s, 
 // 16-entry table of float4 {0 or -inf} that is added to the values (x + 0 =
 // x, x + -inf = -inf for finite x), with no per-element branch; warps with no
 // penalized element in the tile skip it.
+// kCheck = false: tile it is not the row's last, so its octets are in range
+template <bool kCheck = true>
 __device__ __forceinline__ void mask_penalized(const Row& R, const uint8_t* bits8, const float4* lut, float* v,
                                                int it) {
     // the thread's 16 bits (pen_bit order = register order), one 16-bit load
     const int o0 = it * OCT_TILE + 2 * (int)threadIdx.x;
-    const uint32_t m = o0 < R.noct ? *reinterpret_cast<const uint16_t*>(bits8 + o0) : 0u;
+    const uint32_t m = (!kCheck || o0 < R.noct) ? *reinterpret_cast<const uint16_t*>(bits8 + o0) : 0u;
     if (__any_sync(FULL, m != 0u)) {
         const float4 q[4] = {lut[m & 15u], lut[(m >> 4) & 15u], lut[(m >> 8) & 15u], lut[m >> 12]};
 #pragma unroll
@@ -1343,7 +1345,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
         constexpr bool kG1 = decltype(g1)::value;
         auto body = [&](float (&v)[16], int it, auto last) {
             constexpr bool kMaybeLast = decltype(last)::value;
-            if (R.use_pen) mask_penalized(R, bits8, s.pen_lut, v, it);
+            if (R.use_pen) mask_penalized<kMaybeLast>(R, bits8, s.pen_lut, v, it);
             // sample.c:142: sc = l * inv_t, rounded exactly like the reference
             // (packed pairs: each lane is the same IEEE multiply)
             f32x2 sc2[8];
