@@ -1341,11 +1341,13 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
     int next_ck = ck_slot(0), ck = 0;  // next checkpoint slot and its index
     // g1: one tile per table slot (compile-time); last: std::true_type when
     // `it` may be the row's last tile
-    auto run = [&](auto g1) {
+    // pen: the row has penalized ids (compile-time, like g1)
+    auto run = [&](auto g1, auto pen) {
         constexpr bool kG1 = decltype(g1)::value;
+        constexpr bool kPen = decltype(pen)::value;
         auto body = [&](float (&v)[16], int it, auto last) {
             constexpr bool kMaybeLast = decltype(last)::value;
-            if (R.use_pen) mask_penalized<kMaybeLast>(R, bits8, s.pen_lut, v, it);
+            if constexpr (kPen) mask_penalized<kMaybeLast>(R, bits8, s.pen_lut, v, it);
             // sample.c:142: sc = l * inv_t, rounded exactly like the reference
             // (packed pairs: each lane is the same IEEE multiply)
             f32x2 sc2[8];
@@ -1421,8 +1423,13 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
         };
         stream_tiles(R, src, s, body);
     };
-    if (g == 1) run(std::true_type());
-    else run(std::false_type());
+    if (g == 1) {
+        if (R.use_pen) run(std::true_type(), std::true_type());
+        else run(std::true_type(), std::false_type());
+    } else {
+        if (R.use_pen) run(std::false_type(), std::true_type());
+        else run(std::false_type(), std::false_type());
+    }
     if (R.use_pen) {
         csync();
         // the penalized elements join the running max and sum exactly, and
