@@ -139,7 +139,7 @@ int quasar_sampler_pick_batch(const float *d_logits, int64_t ld, int B, int V,
 /* Device workspace one quasar_sampler_pick_batch call of B rows with history
  * capacity hist_cap needs: the per-row summaries the streaming kernel leaves
  * for the finishing kernel (row max and 1/sum, per-thread maxima, tile-max
- * table, penalized-id list; ~20 KB per row at hist_cap 256). Pass
+ * table, penalized-id list; ~15 KB per row at hist_cap 256). Pass
  * d_workspace = NULL to use a workspace the library allocates per device and
  * keeps; that one is shared, so concurrent calls on one device must each
  * pass their own. */
