@@ -177,10 +177,14 @@ __device__ __forceinline__ void lds4(uint32_t addr, float* v) {
                  : "r"(addr)
                  : "memory");
 }
+// The logits are read once: their lines are marked first to go from L2, so
+// they do not push out the per-row summaries the finishing kernel reads.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
     asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-        "l"(src), "r"(bytes), "r"(bar)
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar), "l"(pol)
         : "memory");
 }
 // Asynchronous 4-byte global -> shared copy (cp.async) and its wait.
