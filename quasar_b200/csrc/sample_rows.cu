@@ -2,37 +2,42 @@
 //
 // Replaces franzvill/quasar sample.c:111-178 (quasar_sampler_pick), batched:
 // every row of a [B, V] fp32 logits matrix is sampled exactly as sample.c
-// samples one row, in sample.c's order:
-//   1. history ring -> shared-memory bitset of penalized ids (sample.c:120)
-//   2. ONE pass over the row from HBM: penalty (sample.c:124), temperature scale
-//      (sample.c:137,142), running max, online window sum of exp(sc - running
-//      max) in double (sample.c:147), and a one-byte upper bound of each
-//      thread-tile's max (16 elements) kept in shared memory. Elements more than
-//      30 below the running max contribute < e^-30 each to that sum instead of
-//      being dropped (relative effect < V*e^-30 in the worst case, ~1e-11 on
-//      realistic rows).
-//   3. candidate path (min_p > 0 or top_k <= 256): with the row max known, the
-//      kept prefix lies above a threshold (min-p floor, or the k-th largest
-//      per-thread max); only thread-tiles whose bound clears it are read again (a few % of
-//      the row). Their survivors get exact p = (float)exp(sc - max) *
-//      (float)(1/sum), a bitonic sort by (p desc, id asc) (= glibc's stable
-//      qsort of sample.c:151), then the top-k / top-p / min-p cuts and the
-//      inverse-CDF draw with the row's xorshift64* state (sample.c:153-177).
-//   4. select path (any parameters, or when the candidates exceed 4096): the
-//      row is listed in a workspace and a second kernel runs an exact radix
-//      select over the p keys of the whole row, re-reading it.
-// Greedy rows (temperature <= 0) take one pass: penalized argmax, first index
-// on ties, no PRNG step (sample.c:130-134).
+// samples one row, in sample.c's order, by two kernels.
 //
-// Two main kernels share the per-row code:
+// Kernel A (sample_rows_tma / sample_rows_ldg), one pass over each row:
+//   1. history ring -> shared-memory bitset of penalized ids (sample.c:120);
+//   2. the stream: penalized ids read as -inf, temperature scale (sample.c:
+//      137,142), running max, online window sum of exp(sc - m_ref) with a
+//      lagging reference m_ref, in fp32 per tile and double per row
+//      (sample.c:147), and a one-byte bound of each thread-slot's max (16
+//      contiguous elements) in a workspace table with six checkpoint anchors.
+//      Elements more than 30 below the max contribute < e^-30 each to the sum
+//      instead of being dropped (relative effect < V*e^-30 in the worst case);
+//   3. the penalized ids (sample.c:124, exact IEEE divide / multiply) join the
+//      max and sum and are listed for kernel B; block reductions give the row
+//      max and inv = (float)(1/sum). Greedy rows (temperature <= 0) finish
+//      here: penalized argmax, first index on ties, no PRNG step
+//      (sample.c:130-134).
+// Kernel B (sample_rows_finish), one CTA per stochastic row:
+//   candidate path (min_p > 0 or top_k <= 256): the kept prefix lies above a
+//   threshold known from the max (min-p floor, or the k-th largest per-thread
+//   max); only thread-slots whose bound clears it are read again. Survivors
+//   get exact p = (float)exp(sc - max) * inv, ordered by (p desc, id asc) (=
+//   glibc's stable qsort, sample.c:151) through per-candidate ranks (<= 256
+//   survivors) or a counting sort, then the top-k / top-p / min-p cuts and the
+//   inverse-CDF draw with the row's xorshift64* state (sample.c:153-177);
+//   select path (any parameters, or more than 4096 candidates): an exact radix
+//   select over the p keys of the whole row, re-reading it.
+//
 //   sample_rows_tma  persistent CTAs of 8 consumer warps + 1 producer warp. The
 //                    producer streams the rows' 16 KB chunks with cp.async.bulk
-//                    (TMA, this GPU's own memory only) into a 3-stage shared-memory ring
-//                    guarded by mbarriers, running ahead into the next row
-//                    while the consumers finish the current one. Needs rows
-//                    that start 16-byte aligned and V % 4 == 0.
-//   sample_rows_ldg  one CTA per row, 256-bit register loads with a one-tile
-//                    prefetch; any alignment and V.
+//                    (TMA, this GPU's own memory only, L2 evict-first) into a
+//                    3-stage shared-memory ring guarded by mbarriers, running
+//                    ahead into the next row while the consumers finish the
+//                    current one. Needs rows that start 16-byte aligned and
+//                    V % 4 == 0.
+//   sample_rows_ldg  the same persistent CTAs without the ring: register loads
+//                    with tiles in flight; any alignment and V.
 // Every mbarrier wait is bounded (clock64); a timeout sets the abort flag, the
 // rows report id -1 and the kernel runs to its end.
 #include <float.h>
