@@ -77,6 +77,8 @@ __host__ __device__ constexpr int ck_slot(int k) {
 }
 constexpr int TOPK_MAX = CONSUMERS;            // largest top_k the candidate path takes
 constexpr int QMAX = 4096;                     // qualifying thread-tiles re-read per row
+// a list entry is slot * CONSUMERS + thread, slot < TMAX_TILES: 16 bits hold it
+static_assert(TMAX_TILES * CONSUMERS <= 65536, "16-bit slot-list entries");
 constexpr int NB = 1024;                       // radix bins per level (10 bits)
 constexpr long long WAIT_CYCLES = 1ll << 32;   // ~2 s: bound on any mbarrier wait
 constexpr float REF_SLACK = 64.0f;             // kernel A: exp reference lag (nats), e^64 << FLT_MAX
@@ -217,23 +219,9 @@ __device__ __forceinline__ void ld8(const float* p, float* v) {
                  : "l"(p));
 }
 
-// One 32-byte octet of a row (elements 8o..8o+7) from global memory: a single
-// 256-bit load when the row is 32-byte aligned (sm_100 ld.global.v8), else
-// masked scalar loads; elements past V read as -inf.
-__device__ __forceinline__ void load_oct(const float* row, int o, int V, bool vec, float* v) {
-    const int e = o * 8;
-    if (vec && e + 7 < V) {
-        asm volatile("ld.global.nc.L1::no_allocate.L2::evict_first.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                     : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]),
-                       "=f"(v[6]), "=f"(v[7])
-                     : "l"(row + e));
-    } else {
-#pragma unroll
-        for (int k = 0; k < 8; k++) v[k] = (e + k < V) ? __ldcs(row + e + k) : -INFINITY;
-    }
-}
-
-// The same octet load with the default cache policy (re-reads of a few tiles).
+// One 32-byte octet of a row (elements 8o..8o+7) from global memory with the
+// default cache policy: a single 256-bit load when the row is 32-byte aligned
+// (sm_100 ld.global.v8), else masked scalar loads; elements past V read as -inf.
 __device__ __forceinline__ void load_oct_keep(const float* row, int o, int V, bool vec, float* v) {
     const int e = o * 8;
     if (vec && e + 7 < V) {
@@ -327,20 +315,34 @@ struct Row {
     float rp, inv_t, M, thr, inv;
 };
 
+// Octets in flight per thread in the select path's passes over a row.
+constexpr int SCAN_U = 4;
+
 // Calls f(sc, idx) for every in-range element whose scaled logit lies in
-// [s_lo, s_hi], reading the row from global memory in coalesced octets.
+// [s_lo, s_hi], reading the row from global memory in coalesced octets,
+// SCAN_U loads in flight per thread. The select path passes over the same
+// row up to ten times, so the loads keep the default L2 policy: after the
+// first pass the row is read from L2.
 template <class F>
 __device__ __forceinline__ void scan_row(const Row& R, const uint8_t* bits8, float s_lo, float s_hi,
                                          F&& f) {
-    for (int o = threadIdx.x; o < R.noct; o += CONSUMERS) {
-        float v[8];
-        load_oct(R.ptr, o, R.V, R.vec, v);
-        if (R.use_pen) apply_pen_oct(v, bits8[o], R.rp);
+    for (int ob = threadIdx.x; ob < R.noct; ob += SCAN_U * CONSUMERS) {
+        float v[SCAN_U][8];
 #pragma unroll
-        for (int k = 0; k < 8; k++) {
-            const float sc = __fmul_rn(v[k], R.inv_t);
-            const int idx = 8 * o + k;
-            if (idx < R.V && sc >= s_lo && sc <= s_hi) f(sc, idx);
+        for (int u = 0; u < SCAN_U; u++)
+            if (ob + u * CONSUMERS < R.noct) load_oct_keep(R.ptr, ob + u * CONSUMERS, R.V, R.vec, v[u]);
+#pragma unroll
+        for (int u = 0; u < SCAN_U; u++) {
+            const int o = ob + u * CONSUMERS;
+            if (o < R.noct) {
+                if (R.use_pen) apply_pen_oct(v[u], bits8[o], R.rp);
+#pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    const float sc = __fmul_rn(v[u][k], R.inv_t);
+                    const int idx = 8 * o + k;
+                    if (idx < R.V && sc >= s_lo && sc <= s_hi) f(sc, idx);
+                }
+            }
         }
     }
 }
@@ -505,11 +507,19 @@ __device__ int resolve_id(const Row& R, const uint8_t* bits8, const Sel& sel, Sh
         return idx < R.V && sc >= s_lo && sc <= s_hi && p_key(sc, R.M, R.thr, R.inv) == sel.key;
     };
     int mine = 0;
-    for (int o = o0; o < o1; o++) {
-        float v[8];
-        load_oct(R.ptr, o, R.V, R.vec, v);
-        if (R.use_pen) apply_pen_oct(v, bits8[o], R.rp);
-        for (int k = 0; k < 8; k++) mine += match(v[k], 8 * o + k) ? 1 : 0;
+    for (int ob = o0; ob < o1; ob += SCAN_U) {  // SCAN_U loads in flight
+        float v[SCAN_U][8];
+#pragma unroll
+        for (int u = 0; u < SCAN_U; u++)
+            if (ob + u < o1) load_oct_keep(R.ptr, ob + u, R.V, R.vec, v[u]);
+#pragma unroll
+        for (int u = 0; u < SCAN_U; u++) {
+            if (ob + u < o1) {
+                if (R.use_pen) apply_pen_oct(v[u], bits8[ob + u], R.rp);
+#pragma unroll
+                for (int k = 0; k < 8; k++) mine += match(v[u][k], 8 * (ob + u) + k) ? 1 : 0;
+            }
+        }
     }
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int incl = warp_incl_scan(mine, lane);
@@ -521,7 +531,7 @@ __device__ int resolve_id(const Row& R, const uint8_t* bits8, const Sel& sel, Sh
         int want = sel.t - before;
         for (int o = o0; o < o1 && want >= 0; o++) {
             float v[8];
-            load_oct(R.ptr, o, R.V, R.vec, v);
+            load_oct_keep(R.ptr, o, R.V, R.vec, v);
             if (R.use_pen) apply_pen_oct(v, bits8[o], R.rp);
             for (int k = 0; k < 8 && want >= 0; k++) {
                 if (match(v[k], 8 * o + k)) {
@@ -1505,7 +1515,7 @@ __device__ __forceinline__ void shard_norm(const RowsArgs& a, int row, float& M,
 }
 
 __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t* buf, uint32_t* bits,
-                                           Buckets* bk, Shared& s) {
+                                           Buckets* bk, uint16_t* qlist, Shared& s) {
     const int tid = threadIdx.x, lane = tid & 31;
     const uint8_t* bits8 = reinterpret_cast<const uint8_t*>(bits);
     // every global load of the row - parameters, ring state and kernel A's
@@ -1579,7 +1589,7 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
             tau = fmaxf(tau, topk_floor(P.top_k, s));
         }
         const float lo = fmaxf(tau, R.thr);
-        // qualifying thread-slots -> a shared list (bottom of buf), so the
+        // qualifying thread-slots -> a shared list (its own area), so the
         // re-reads spread over all threads; positions from a block scan
         // A slot qualifies when thread max - (anchor + slot deficit)/8 >= lo,
         // i.e. anchor + deficit <= X = floor(8 (max - lo)) (+1 of slack, so
@@ -1630,11 +1640,10 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
             if (w < (tid >> 5)) off += s.ri[w];
             nq_all += s.ri[w];
         }
-        uint32_t* qlist = reinterpret_cast<uint32_t*>(buf);
         for (; qmask; qmask &= qmask - 1ull, off++)
-            if (off < QMAX) qlist[off] = (uint32_t)((__ffsll((long long)qmask) - 1) * CONSUMERS + tid);
+            if (off < QMAX) qlist[off] = (uint16_t)((__ffsll((long long)qmask) - 1) * CONSUMERS + tid);
         const int nq = min(nq_all, QMAX);
-        const int room = CAP - (nq + 1) / 2;  // entries left above the list
+        const int room = CAP;  // the list has its own area: every candidate entry is free
         // raw survivors are appended from the top of buf downwards: first the
         // penalized ids that clear the threshold
         for (int i = tid; i < npen; i += CONSUMERS) {
@@ -1775,7 +1784,8 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
 // ---------------------------------------------------------------------------
 // Kernels. Dynamic shared memory: kernel A row-load variant [bits]; kernel A
 // ring variant [to 64 B][ring NSTAGE x 16 KB][bits][full bars][empty bars]; kernel B
-// [scratch: candidate keys / select histograms][bits][counting-sort buckets].
+// [scratch: candidate keys / select histograms][bits][counting-sort buckets]
+// [qualifying-slot list: QMAX 16-bit entries].
 
 __global__ void __launch_bounds__(CONSUMERS, QS_A_CTAS) sample_rows_ldg(RowsArgs a) {
     extern __shared__ __align__(128) unsigned char dyn[];
@@ -1863,7 +1873,8 @@ __global__ void __launch_bounds__(CONSUMERS, 3) sample_rows_finish(RowsArgs a) {
     uint32_t* bits = reinterpret_cast<uint32_t*>(dyn + FINISH_SCRATCH);
     Buckets* bk = reinterpret_cast<Buckets*>(dyn + FINISH_SCRATCH + (((size_t)a.nwords * 4 + 15) & ~(size_t)15));
     __shared__ Shared s;
-    if ((int)blockIdx.x < a.B) finish_row(a, blockIdx.x, buf, bits, bk, s);  // one row per CTA
+    uint16_t* qlist = reinterpret_cast<uint16_t*>(reinterpret_cast<unsigned char*>(bk) + sizeof(Buckets));
+    if ((int)blockIdx.x < a.B) finish_row(a, blockIdx.x, buf, bits, bk, qlist, s);  // one row per CTA
 }
 
 // Merge of the vocab shards' candidates, one CTA per row: the G*k gathered
@@ -1927,8 +1938,9 @@ size_t rows_tma_smem_bytes(int V) {  // kernel A, ring variant (+64: ring alignm
            2 * rows::NSTAGE * sizeof(uint64_t);
 }
 
-size_t rows_finish_smem_bytes(int V) {  // kernel B: [scratch][bits][buckets]
-    return (size_t)rows::FINISH_SCRATCH + (((size_t)nwords_for(V) * 4 + 15) & ~(size_t)15) + sizeof(rows::Buckets);
+size_t rows_finish_smem_bytes(int V) {  // kernel B: [scratch][bits][buckets][slot list]
+    return (size_t)rows::FINISH_SCRATCH + (((size_t)nwords_for(V) * 4 + 15) & ~(size_t)15) + sizeof(rows::Buckets) +
+           rows::QMAX * sizeof(uint16_t);
 }
 
 // [abort word][pad][info B x float4][tfmax B x 256 floats][penalized list B x
