@@ -102,6 +102,30 @@ def test_config3_exact_select_agrees():
     assert_parity(ids_s, diag_s, rng_s, res, rng_ref)
 
 
+def test_large_candidate_lists_stay_on_candidate_path():
+    """Rows with 2200-3400 candidates spread over about as many thread-slots
+    (the flat top a history full of recently chosen tokens gives under a
+    repeat penalty): the candidate path takes every one of them, without the
+    select path's whole-row passes, and matches the reference. Per-row min_p
+    puts the min-p floor halfway between the k-th and (k+1)-th largest scaled
+    logits, away from any tie."""
+    B = 32
+    T = 1.5
+    logits, hist = gpu_inputs(O.SYNTH_NORMAL, 17, B, V_FULL, 3.0, H=64, hist_seed=18)
+    sc = np.sort(logits.cpu().numpy() / np.float32(T), axis=1)[:, ::-1]
+    k = np.linspace(2200, 3400, B).astype(np.int64)
+    mid = 0.5 * (sc[np.arange(B), k - 1].astype(np.float64) + sc[np.arange(B), k])
+    min_p = np.exp(mid - sc[:, 0]).astype(np.float32)
+    prm = O.make_params(B, temperature=T, top_p=1.0, min_p=min_p, repeat_penalty=1.1)
+    seeds = _seeds(B, 700)
+    ids, diag, rng = run_gpu(logits, prm, seeds, hist=hist)
+    res, rng_ref = run_oracle(logits, prm, seeds, hist=hist)
+    # (a few of these rows draw within 1e-6 of a CDF or tie boundary)
+    assert_parity(ids, diag, rng, res, rng_ref, max_mismatch_frac=0.1)
+    assert (diag["path"] == 1).all(), np.bincount(diag["path"])
+    assert (res["n_kept"] > 2048).all(), res["n_kept"]
+
+
 def test_config5_subset_zipf():
     B = 96
     logits, hist = gpu_inputs(O.SYNTH_ZIPF, 5, B, V_FULL, 1.1, H=2048, hist_seed=55)
