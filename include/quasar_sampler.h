@@ -40,8 +40,11 @@ typedef struct quasar_sampler quasar_sampler;
 
 /* Replaces sample.h:14 / sample.c:31-39. Defaults: greedy (temperature 0),
  * top_p 1, top_k 0, min_p 0, repeat_penalty 1, repeat_last_n 0, PRNG state
- * 0x9E3779B97F4A7C15. Device buffers are allocated lazily on the current CUDA
- * device. Returns NULL when the host allocation fails. */
+ * 0x9E3779B97F4A7C15. Device buffers - PRNG word, history ring and the
+ * object's own kernel workspace, like the per-object scratch of
+ * sample.c:94-104 - are allocated lazily on the current CUDA device and used
+ * on the object's own stream, so distinct objects can pick concurrently from
+ * different host threads. Returns NULL when the host allocation fails. */
 quasar_sampler *quasar_sampler_new(void);
 
 /* Replaces sample.h:15 / sample.c:41-45. NULL-safe. */
@@ -140,9 +143,11 @@ int quasar_sampler_pick_batch(const float *d_logits, int64_t ld, int B, int V,
  * capacity hist_cap needs: the per-row summaries the streaming kernel leaves
  * for the finishing kernel (row max and 1/sum, per-thread maxima, tile-max
  * table, penalized-id list; ~15 KB per row at hist_cap 256). Pass
- * d_workspace = NULL to use a workspace the library allocates per device and
- * keeps; that one is shared, so concurrent calls on one device must each
- * pass their own. */
+ * d_workspace = NULL to use a workspace the library allocates and keeps per
+ * (device, stream): calls on different streams never share one, and calls on
+ * one stream are ordered by it. It grows with stream-ordered allocations
+ * (cudaMallocAsync / cudaFreeAsync on that stream), never a device-wide
+ * synchronisation. */
 size_t quasar_sampler_workspace_bytes(int B, int hist_cap);
 
 /* Kernel launches one quasar_sampler_pick_batch call makes (2: the streaming
@@ -169,8 +174,11 @@ int quasar_sampler_pick_batch_launches(void);
  * on one device in the process: calls that overlap (two streams or threads)
  * race on it and must be serialised by the caller. The first call on each
  * device sets up (array address lookup, kernel attributes); make it before any
- * stream capture. Every call clears the one word that must start at zero (the
- * abort flag) with a memset on `stream`. */
+ * stream capture. The array's address is looked up once per device and kept,
+ * so do not use this entry point across a cudaDeviceReset. Arguments are
+ * checked as quasar_sampler_pick_batch checks them, before the size check.
+ * Every call clears the one word that must start at zero (the abort flag)
+ * with a memset on `stream`. */
 int quasar_sampler_pick_batch_noalloc(const float *d_logits, int64_t ld, int B, int V,
                                       const quasar_sample_params *d_params,
                                       const quasar_sample_params *h_params,

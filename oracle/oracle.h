@@ -95,6 +95,19 @@ QS_API int qs_ref_sequence(const float *logits, int64_t ld, int n_steps, int V,
                     const qs_params *prm, int repeat_last_n, uint64_t seed,
                     int32_t *ids_out);
 
+/* The decode loop of a batch: row r gets its own reference object (set up as
+ * qs_ref_pick_rows sets it up) and is picked n_steps times on the same logits
+ * row, each choice recorded in its ring (sample.c:83-92), as a server that
+ * keeps re-sampling would drive it. res is [n_steps][B]; rng[] ends at the
+ * final states; hist_out [B][hist_cap], len_out [B] and head_out [B] (may be
+ * NULL) get the final rings. */
+QS_API int qs_ref_decode(const float *logits, int64_t ld, int B, int V,
+                  const qs_params *params, int per_row_params,
+                  const int32_t *hist, int hist_cap,
+                  const int32_t *hist_len, const int32_t *hist_head,
+                  uint64_t *rng, int n_steps, qs_result *res,
+                  int32_t *hist_out, int32_t *len_out, int32_t *head_out, int nthreads);
+
 /* ---- synthetic inputs (both builds; synth.c) ------------------------------ */
 
 enum { QS_SYNTH_NORMAL = 0, QS_SYNTH_GUMBEL_PEAK = 1, QS_SYNTH_ZIPF = 2 };

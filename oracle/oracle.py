@@ -70,6 +70,9 @@ def _lib(backend: str) -> ctypes.CDLL:
             lib.qs_ref_sequence.argtypes = [P, ctypes.c_int64, ctypes.c_int, ctypes.c_int, P,
                                             ctypes.c_int, ctypes.c_uint64, P]
             lib.qs_ref_sequence.restype = ctypes.c_int
+            lib.qs_ref_decode.argtypes = [P, ctypes.c_int64, ctypes.c_int, ctypes.c_int, P, ctypes.c_int,
+                                          P, ctypes.c_int, P, P, P, ctypes.c_int, P, P, P, P, ctypes.c_int]
+            lib.qs_ref_decode.restype = ctypes.c_int
         _libs[backend] = lib
     return _libs[backend]
 
@@ -129,6 +132,33 @@ def ref_sequence(logits: np.ndarray, params: np.ndarray, repeat_last_n: int, see
     if rc != 0:
         raise RuntimeError(f"ref_sequence failed: {rc}")
     return out
+
+
+def ref_decode(logits: np.ndarray, params: np.ndarray, rng: np.ndarray, n_steps: int,
+               hist: np.ndarray, hist_len: np.ndarray, hist_head: np.ndarray,
+               nthreads: int | None = None):
+    """A decode loop through the reference: row r gets one sampler object with
+    its own ring and seed, picked n_steps times on the same logits row with each
+    choice recorded. Returns (results [n_steps, B], rng_after, hist, len, head)."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    B, V = logits.shape
+    params = np.ascontiguousarray(params, dtype=PARAMS_DTYPE)
+    per_row = 1 if params.shape[0] == B and B > 1 else 0
+    rng = np.array(rng, dtype=np.uint64).reshape(B).copy()
+    hist = np.ascontiguousarray(hist, dtype=np.int32).reshape(B, -1)
+    cap = hist.shape[1]
+    hist_len = np.ascontiguousarray(hist_len, dtype=np.int32).reshape(B)
+    hist_head = np.ascontiguousarray(hist_head, dtype=np.int32).reshape(B)
+    res = np.zeros((n_steps, B), dtype=RESULT_DTYPE)
+    h_out = np.zeros_like(hist)
+    l_out = np.zeros(B, dtype=np.int32)
+    d_out = np.zeros(B, dtype=np.int32)
+    rc = _lib("ref").qs_ref_decode(_ptr(logits), V, B, V, _ptr(params), per_row, _ptr(hist), cap,
+                                   _ptr(hist_len), _ptr(hist_head), _ptr(rng), int(n_steps), _ptr(res),
+                                   _ptr(h_out), _ptr(l_out), _ptr(d_out), nthreads or os.cpu_count() or 1)
+    if rc != 0:
+        raise RuntimeError(f"ref_decode failed: {rc}")
+    return res, rng, h_out, l_out, d_out
 
 
 def synth_logits(kind: int, seed: int, row0: int, B: int, V: int, scale: float = 1.0,

@@ -10,7 +10,9 @@
 #include <string.h>
 #include <time.h>
 
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "../../include/quasar_sampler.h"
 #include "sample_rows.cuh"
@@ -32,33 +34,62 @@ struct quasar_sampler {
     float* d_logits;
     int logits_cap;
     int32_t* h_id;  // pinned
+    void* d_ws;     // this object's kernel workspace (stream-ordered allocation)
+    size_t ws_bytes;
     int last_error;
 };
 
 namespace {
 
-// Workspace the library keeps per device for callers that pass none.
-std::mutex g_ws_mu;
-void* g_ws[64];
-size_t g_ws_bytes[64];
+// Workspaces the library keeps for quasar_sampler_pick_batch callers that pass
+// none: one per (device, stream), so calls on different streams never share
+// one, and calls on one stream are ordered by the stream. Growth frees the old
+// buffer stream-ordered (cudaFreeAsync after the work already queued on that
+// stream) and allocates the new one the same way, so it never waits for the
+// device. The mutex is held until the launch is queued, so a concurrent grow
+// on the same stream cannot free a buffer another thread is about to use.
+struct ManagedWs {
+    void* ptr;     // allocation
+    size_t bytes;  // usable bytes from align256(ptr)
+};
 
-int managed_workspace(size_t bytes, void** out) {
+// Workspaces must start on a 256-byte boundary; allocations get 256 bytes of
+// slack and are used from the first aligned address.
+void* align256(void* p) { return (void*)(((uintptr_t)p + 255) & ~(uintptr_t)255); }
+std::mutex g_ws_mu;
+std::map<std::pair<int, uintptr_t>, ManagedWs> g_ws;
+
+int managed_workspace(size_t bytes, cudaStream_t stream, void** out) {
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return QUASAR_ECUDA;
-    std::lock_guard<std::mutex> lock(g_ws_mu);
-    if (g_ws_bytes[dev] < bytes) {
-        if (g_ws[dev]) {
-            // a previous call may still read it
-            if (cudaDeviceSynchronize() != cudaSuccess) return QUASAR_ECUDA;
-            cudaFree(g_ws[dev]);
-            g_ws[dev] = nullptr;
-            g_ws_bytes[dev] = 0;
-        }
+    if (cudaGetDevice(&dev) != cudaSuccess) return QUASAR_ECUDA;
+    ManagedWs& w = g_ws[std::make_pair(dev, (uintptr_t)stream)];
+    if (w.bytes < bytes) {
+        if (w.ptr && cudaFreeAsync(w.ptr, stream) != cudaSuccess) return QUASAR_ECUDA;
+        w.ptr = nullptr;
+        w.bytes = 0;
         const size_t grow = bytes < ((size_t)1 << 16) ? ((size_t)1 << 16) : bytes;
-        if (cudaMalloc(&g_ws[dev], grow) != cudaSuccess) return QUASAR_ENOMEM;
-        g_ws_bytes[dev] = grow;
+        if (cudaMallocAsync(&w.ptr, grow + 256, stream) != cudaSuccess) {
+            w.ptr = nullptr;
+            return QUASAR_ENOMEM;
+        }
+        w.bytes = grow;
     }
-    *out = g_ws[dev];
+    *out = align256(w.ptr);
+    return QUASAR_OK;
+}
+
+// Grows a sampler object's own workspace on its own stream (sample.c:94-104
+// keeps scratch per object the same way).
+int object_workspace(quasar_sampler* s, size_t bytes) {
+    if (s->ws_bytes >= bytes) return QUASAR_OK;
+    if (s->d_ws && cudaFreeAsync(s->d_ws, s->stream) != cudaSuccess) return QUASAR_ECUDA;
+    s->d_ws = nullptr;
+    s->ws_bytes = 0;
+    if (cudaMallocAsync(&s->d_ws, bytes + 256, s->stream) != cudaSuccess) {
+        s->d_ws = nullptr;
+        return QUASAR_ENOMEM;
+    }
+    s->ws_bytes = bytes;
     return QUASAR_OK;
 }
 
@@ -94,16 +125,22 @@ int sync_config(quasar_sampler* s) {
     // sample.c:61-66: the ring is reallocated only for a new nonzero capacity;
     // repeat_last_n = 0 keeps an existing ring (and its recording) in place.
     if (s->repeat_last_n > 0 && s->repeat_last_n != s->hist_cap) {
-        if (s->d_hist) cudaFree(s->d_hist);
+        if (s->d_hist && cudaFreeAsync(s->d_hist, s->stream) != cudaSuccess) return QUASAR_ECUDA;
         s->d_hist = nullptr;
         s->hist_cap = 0;
-        if (cudaMalloc(&s->d_hist, (size_t)s->repeat_last_n * sizeof(int32_t)) != cudaSuccess)
+        if (cudaMallocAsync((void**)&s->d_hist, (size_t)s->repeat_last_n * sizeof(int32_t), s->stream) !=
+            cudaSuccess) {
+            s->d_hist = nullptr;
             return QUASAR_ENOMEM;
+        }
         if (cudaMemsetAsync(s->d_hist, 0, (size_t)s->repeat_last_n * sizeof(int32_t),
                             s->stream) != cudaSuccess)
             return QUASAR_ECUDA;
         s->hist_cap = s->repeat_last_n;
     }
+    // this object's own workspace for a one-row pick with its ring
+    rc = object_workspace(s, qs::rows_workspace_bytes(1, s->hist_cap));
+    if (rc != QUASAR_OK) return rc;
     if (s->rng_dirty) {
         if (cudaMemcpyAsync(s->d_rng, &s->seed_state, sizeof(uint64_t), cudaMemcpyHostToDevice,
                             s->stream) != cudaSuccess)
@@ -116,6 +153,28 @@ int sync_config(quasar_sampler* s) {
 }
 
 }  // namespace
+
+namespace qs {
+
+bool rows_tma_ok(const float* d_logits, int64_t ld, int V) {
+    return ((uintptr_t)d_logits % 16 == 0) && (ld % 4 == 0) && (V % 4 == 0) &&
+           rows_tma_smem_bytes(V) <= 220 * 1024;
+}
+
+int check_pick_batch_args(const float* d_logits, int64_t ld, int B, int V, const quasar_sample_params* d_params,
+                          const quasar_sample_params* h_params, const uint64_t* d_rng, const int32_t* d_hist,
+                          int hist_cap, const int32_t* d_hist_len, const int32_t* d_hist_head, int record,
+                          const int32_t* d_out) {
+    if (B < 0 || V < 1 || V > QUASAR_MAX_VOCAB || ld < V) return QUASAR_EINVAL;
+    if (B == 0) return QUASAR_OK;
+    if (!d_logits || !d_rng || !d_out || (!d_params && !h_params)) return QUASAR_EINVAL;
+    if (hist_cap < 0 || (hist_cap > 0 && !d_hist)) return QUASAR_EINVAL;
+    if (record && hist_cap > 0 && (!d_hist_len || !d_hist_head)) return QUASAR_EINVAL;
+    if (!rows_tma_ok(d_logits, ld, V) && rows_smem_bytes(V) > 220 * 1024) return QUASAR_EUNSUPPORTED;
+    return QUASAR_OK;
+}
+
+}  // namespace qs
 
 extern "C" {
 
@@ -145,14 +204,9 @@ int quasar_sampler_pick_batch(const float* d_logits, int64_t ld, int B, int V,
                               int32_t* d_hist_head, int record, int32_t* d_out,
                               quasar_pick_diag* d_diag, void* d_workspace, size_t workspace_bytes,
                               int flags, void* stream) {
-    if (B < 0 || V < 1 || V > QUASAR_MAX_VOCAB || ld < V) return QUASAR_EINVAL;
-    if (B == 0) return QUASAR_OK;
-    if (!d_logits || !d_rng || !d_out || (!d_params && !h_params)) return QUASAR_EINVAL;
-    if (hist_cap < 0 || (hist_cap > 0 && !d_hist)) return QUASAR_EINVAL;
-    if (record && hist_cap > 0 && (!d_hist_len || !d_hist_head)) return QUASAR_EINVAL;
-    const bool tma = ((uintptr_t)d_logits % 16 == 0) && (ld % 4 == 0) && (V % 4 == 0) &&
-                     qs::rows_tma_smem_bytes(V) <= 220 * 1024;
-    if (!tma && qs::rows_smem_bytes(V) > 220 * 1024) return QUASAR_EUNSUPPORTED;
+    const int rc = qs::check_pick_batch_args(d_logits, ld, B, V, d_params, h_params, d_rng, d_hist, hist_cap,
+                                             d_hist_len, d_hist_head, record, d_out);
+    if (rc != QUASAR_OK || B == 0) return rc;
     qs::RowsArgs a;
     memset(&a, 0, sizeof a);
     a.logits = d_logits;
@@ -171,17 +225,18 @@ int quasar_sampler_pick_batch(const float* d_logits, int64_t ld, int B, int V,
     a.diag = d_diag;
     a.flags = flags;
     a.vec = ((uintptr_t)d_logits % 32 == 0) && (ld % 8 == 0);
-    a.tma = tma && !(flags & QUASAR_FLAG_NO_TMA);
-    void* ws = d_workspace;
-    if (ws) {
-        if (workspace_bytes < qs::rows_workspace_bytes(B, hist_cap) || (uintptr_t)ws % 256 != 0)
+    a.tma = qs::rows_tma_ok(d_logits, ld, V) && !(flags & QUASAR_FLAG_NO_TMA);
+    const cudaStream_t st = (cudaStream_t)stream;
+    if (d_workspace) {
+        if (workspace_bytes < qs::rows_workspace_bytes(B, hist_cap) || (uintptr_t)d_workspace % 256 != 0)
             return QUASAR_EINVAL;
-    } else {
-        const int rc = managed_workspace(qs::rows_workspace_bytes(B, hist_cap), &ws);
-        if (rc != QUASAR_OK) return rc;
+        return qs::launch_sample_rows(a, d_workspace, st) == cudaSuccess ? QUASAR_OK : QUASAR_ECUDA;
     }
-    const cudaError_t err = qs::launch_sample_rows(a, ws, (cudaStream_t)stream);
-    return err == cudaSuccess ? QUASAR_OK : QUASAR_ECUDA;
+    std::lock_guard<std::mutex> lock(g_ws_mu);  // held until the launch is queued
+    void* ws = nullptr;
+    const int wrc = managed_workspace(qs::rows_workspace_bytes(B, hist_cap), st, &ws);
+    if (wrc != QUASAR_OK) return wrc;
+    return qs::launch_sample_rows(a, ws, st) == cudaSuccess ? QUASAR_OK : QUASAR_ECUDA;
 }
 
 quasar_sampler* quasar_sampler_new(void) {
@@ -204,11 +259,12 @@ void quasar_sampler_free(quasar_sampler* s) {
         int dev = 0;
         cudaGetDevice(&dev);
         if (dev != s->device) cudaSetDevice(s->device);
+        if (s->d_ws) cudaFreeAsync(s->d_ws, s->stream);
+        if (s->d_hist) cudaFreeAsync(s->d_hist, s->stream);
+        if (s->d_logits) cudaFreeAsync(s->d_logits, s->stream);
         cudaStreamSynchronize(s->stream);
         cudaFree(s->d_rng);
         cudaFree(s->d_meta);
-        cudaFree(s->d_hist);
-        cudaFree(s->d_logits);
         cudaFreeHost(s->h_id);
         cudaStreamDestroy(s->stream);
         if (dev != s->device) cudaSetDevice(dev);
@@ -263,11 +319,14 @@ int quasar_sampler_pick(quasar_sampler* s, const float* logits, int n_vocab) {
     cudaGetLastError();  // clear a benign error from the attribute query
     if (!on_device) {
         if (s->logits_cap < n_vocab) {
-            cudaFree(s->d_logits);
+            if (s->d_logits && cudaFreeAsync(s->d_logits, s->stream) != cudaSuccess)
+                return set_err(s, QUASAR_ECUDA), -1;
             s->d_logits = nullptr;
             s->logits_cap = 0;
-            if (cudaMalloc(&s->d_logits, (size_t)n_vocab * sizeof(float)) != cudaSuccess)
+            if (cudaMallocAsync((void**)&s->d_logits, (size_t)n_vocab * sizeof(float), s->stream) != cudaSuccess) {
+                s->d_logits = nullptr;
                 return set_err(s, QUASAR_ENOMEM), -1;
+            }
             s->logits_cap = n_vocab;
         }
         if (cudaMemcpyAsync(s->d_logits, logits, (size_t)n_vocab * sizeof(float),
@@ -284,7 +343,7 @@ int quasar_sampler_pick(quasar_sampler* s, const float* logits, int n_vocab) {
     p.reserved = 0;
     rc = quasar_sampler_pick_batch(d_in, n_vocab, 1, n_vocab, nullptr, &p, s->d_rng, s->d_hist,
                                    s->hist_cap, s->d_meta, s->d_meta + 1, 1, s->d_meta + 2,
-                                   nullptr, nullptr, 0, 0, s->stream);
+                                   nullptr, align256(s->d_ws), s->ws_bytes, 0, s->stream);
     if (rc != QUASAR_OK) return set_err(s, rc), -1;
     if (cudaMemcpyAsync(s->h_id, s->d_meta + 2, sizeof(int32_t), cudaMemcpyDeviceToHost,
                         s->stream) != cudaSuccess ||

@@ -17,7 +17,11 @@
 // threads) would share it and corrupt each other's summaries: callers
 // serialise them. The first call on a device looks the array's address up
 // (cudaGetSymbolAddress) and sets the kernels' shared-memory attributes; that
-// set-up belongs before any stream capture. The one workspace word that must
+// set-up belongs before any stream capture. The address is kept for the life
+// of the process: after a cudaDeviceReset the module (and the array) may be
+// loaded elsewhere, so this entry point must not be used across a device
+// reset. Arguments are checked exactly as quasar_sampler_pick_batch checks
+// them (QUASAR_EINVAL / QUASAR_EUNSUPPORTED) before the size check. The one workspace word that must
 // be zero when the kernels start, the abort flag, is cleared by every call
 // with a cudaMemsetAsync on the caller's stream (a memset, not an allocation);
 // every other byte is written by the streaming kernel before the finishing
@@ -27,6 +31,7 @@
 #include <mutex>
 
 #include "../../include/quasar_sampler.h"
+#include "sample_rows.cuh"
 
 namespace {
 
@@ -44,8 +49,10 @@ extern "C" int quasar_sampler_pick_batch_noalloc(const float* d_logits, int64_t 
                                                  int32_t* d_hist, int hist_cap, int32_t* d_hist_len,
                                                  int32_t* d_hist_head, int record, int32_t* d_out,
                                                  quasar_pick_diag* d_diag, int flags, void* stream) {
-    if (B < 0 || hist_cap < 0) return QUASAR_EINVAL;
-    if (B == 0) return QUASAR_OK;
+    // the same argument checks as quasar_sampler_pick_batch, before the size check
+    const int rc = qs::check_pick_batch_args(d_logits, ld, B, V, d_params, h_params, d_rng, d_hist, hist_cap,
+                                             d_hist_len, d_hist_head, record, d_out);
+    if (rc != QUASAR_OK || B == 0) return rc;
     if (quasar_sampler_workspace_bytes(B, hist_cap) > (size_t)QUASAR_NOALLOC_WORKSPACE_BYTES)
         return QUASAR_EOVERFLOW;
     int dev = 0;

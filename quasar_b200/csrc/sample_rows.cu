@@ -43,6 +43,8 @@
 #include <float.h>
 #include <math.h>
 
+#include <atomic>
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -80,6 +82,11 @@ constexpr int QMAX = 4096;                     // qualifying thread-tiles re-rea
 // a list entry is slot * CONSUMERS + thread, slot < TMAX_TILES: 16 bits hold it
 static_assert(TMAX_TILES * CONSUMERS <= 65536, "16-bit slot-list entries");
 constexpr int NB = 1024;                       // radix bins per level (10 bits)
+// Candidates of a min-p row that kernel A lists while it streams (entries
+// (scaled logit bits << 32) | id, every element above the CTA's running
+// min-p threshold): a superset of the row's min-p survivors. A row whose
+// list would exceed it is finished from the tile tables instead.
+constexpr int LIST_CAP = 2048;
 constexpr long long WAIT_CYCLES = 1ll << 32;   // ~2 s: bound on any mbarrier wait
 constexpr float REF_SLACK = 64.0f;             // kernel A: exp reference lag (nats), e^64 << FLT_MAX
 #ifndef QS_LDG_DEPTH
@@ -139,6 +146,10 @@ struct SharedA : Shared {
     // parameters and ring position; its first CONSUMERS ring slots go to tfmax
     quasar_sample_params nxt_pr;
     int nxt_len, nxt_head;
+    // candidate listing of min-p rows: the CTA's running max (ord_key) and
+    // the entries appended so far
+    unsigned int cmax;
+    int nlist;
 };
 
 // Barrier of the 256 consumer threads (warps 0-7); the TMA producer warp never
@@ -1954,28 +1965,37 @@ size_t rows_workspace_bytes(int B, int hist_cap) {
 int rows_threads() { return rows::CONSUMERS; }
 
 namespace {
+// Per-device launch set-up of one kernel (dynamic shared-memory attribute and
+// resident-CTA count), shared by every host thread of the process: the first
+// launch on a device does it under the mutex, later launches read it.
 struct KernelCfg {
-    size_t smem_set[64];
-    int grid[64];  // resident CTAs of the kernel on each device
+    std::atomic<size_t> smem_set[64];
+    std::atomic<int> grid[64];  // resident CTAs of the kernel on each device
 };
-thread_local KernelCfg g_ldg = {}, g_tma = {}, g_fin = {}, g_merge = {};
+KernelCfg g_ldg, g_tma, g_fin, g_merge;
+std::mutex g_cfg_mu;
 
-cudaError_t configure(KernelCfg& cfg, const void* fn, int threads, size_t smem, int dev) {
+cudaError_t configure(KernelCfg& cfg, const void* fn, int threads, size_t smem, int dev, int& grid) {
+    grid = cfg.grid[dev].load(std::memory_order_acquire);
+    if (grid > 0 && cfg.smem_set[dev].load(std::memory_order_acquire) >= smem) return cudaSuccess;
+    std::lock_guard<std::mutex> lock(g_cfg_mu);
     cudaError_t err = cudaSuccess;
-    if (cfg.smem_set[dev] < smem) {
+    if (cfg.smem_set[dev].load() < smem) {
         err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (err != cudaSuccess) return err;
-        cfg.smem_set[dev] = smem;
-        cfg.grid[dev] = 0;
+        // the CTA count below is for the larger carve-out
+        cfg.grid[dev].store(0);
+        cfg.smem_set[dev].store(smem, std::memory_order_release);
     }
-    if (cfg.grid[dev] == 0) {
+    if (cfg.grid[dev].load() == 0) {
         int per_sm = 0, sms = 0;
-        err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem);
+        err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, cfg.smem_set[dev].load());
         if (err != cudaSuccess) return err;
         err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (err != cudaSuccess) return err;
-        cfg.grid[dev] = max(1, per_sm) * sms;
+        cfg.grid[dev].store(max(1, per_sm) * sms, std::memory_order_release);
     }
+    grid = cfg.grid[dev].load();
     return cudaSuccess;
 }
 }  // namespace
@@ -2012,14 +2032,16 @@ cudaError_t launch_stream(const RowsArgs& a, int dev, cudaStream_t stream) {
     if (err != cudaSuccess) return err;
     if (a.tma) {
         const size_t smem = rows_tma_smem_bytes(a.V);
-        err = configure(g_tma, (const void*)rows::sample_rows_tma, rows::CONSUMERS + 32, smem, dev);
+        int grid = 0;
+        err = configure(g_tma, (const void*)rows::sample_rows_tma, rows::CONSUMERS + 32, smem, dev, grid);
         if (err != cudaSuccess) return err;
-        rows::sample_rows_tma<<<min(a.B, g_tma.grid[dev]), rows::CONSUMERS + 32, smem, stream>>>(a);
+        rows::sample_rows_tma<<<min(a.B, grid), rows::CONSUMERS + 32, smem, stream>>>(a);
     } else {
         const size_t smem = rows_smem_bytes(a.V);
-        err = configure(g_ldg, (const void*)rows::sample_rows_ldg, rows::CONSUMERS, smem, dev);
+        int grid = 0;
+        err = configure(g_ldg, (const void*)rows::sample_rows_ldg, rows::CONSUMERS, smem, dev, grid);
         if (err != cudaSuccess) return err;
-        rows::sample_rows_ldg<<<min(a.B, g_ldg.grid[dev]), rows::CONSUMERS, smem, stream>>>(a);
+        rows::sample_rows_ldg<<<min(a.B, grid), rows::CONSUMERS, smem, stream>>>(a);
     }
     return cudaGetLastError();
 }
@@ -2027,7 +2049,8 @@ cudaError_t launch_stream(const RowsArgs& a, int dev, cudaStream_t stream) {
 // Kernel B: one CTA per row.
 cudaError_t launch_finish(const RowsArgs& a, int dev, cudaStream_t stream) {
     const size_t fsmem = rows_finish_smem_bytes(a.V);
-    cudaError_t err = configure(g_fin, (const void*)rows::sample_rows_finish, rows::CONSUMERS, fsmem, dev);
+    int grid = 0;  // unused: one CTA per row
+    cudaError_t err = configure(g_fin, (const void*)rows::sample_rows_finish, rows::CONSUMERS, fsmem, dev, grid);
     if (err != cudaSuccess) return err;
     rows::sample_rows_finish<<<a.B, rows::CONSUMERS, fsmem, stream>>>(a);
     return cudaGetLastError();
@@ -2074,9 +2097,10 @@ cudaError_t launch_shard_merge(const RowsArgs& args, cudaStream_t stream) {
     cudaError_t err = current_device(dev);
     if (err != cudaSuccess) return err;
     const size_t smem = rows_merge_smem_bytes(args.shard_G, args.shard_k);
-    err = configure(g_merge, (const void*)rows::sample_rows_merge, rows::CONSUMERS, smem, dev);
+    int grid = 0;
+    err = configure(g_merge, (const void*)rows::sample_rows_merge, rows::CONSUMERS, smem, dev, grid);
     if (err != cudaSuccess) return err;
-    rows::sample_rows_merge<<<min(args.B, g_merge.grid[dev]), rows::CONSUMERS, smem, stream>>>(args);
+    rows::sample_rows_merge<<<min(args.B, grid), rows::CONSUMERS, smem, stream>>>(args);
     return cudaGetLastError();
 }
 

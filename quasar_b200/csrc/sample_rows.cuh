@@ -34,6 +34,7 @@ struct RowsArgs {
     int2* work_pen;         // [B][hist_cap] (id, scaled penalized logit as int bits)
     uint8_t* work_tmax;     // [B][TMAX] tile-max deficits
     uint8_t* work_anc;      // [B][NCK][256] checkpoint deficits below the thread's final max
+    uint64_t* work_list;    // [B][LIST_CAP] min-p candidates kernel A collected while streaming
     // vocab shards (quasar_shard_*): this matrix holds global columns
     // [col0, col0 + V); kernel A publishes per-row stats instead of finishing
     // greedy rows, and the finishing kernel emits candidate keys
@@ -49,6 +50,15 @@ size_t rows_tma_smem_bytes(int V);  // persistent bulk-copy ring kernel
 size_t rows_finish_smem_bytes(int V);
 size_t rows_workspace_bytes(int B, int hist_cap);  // device workspace of one launch
 int rows_threads();
+// Rows that the bulk-copy ring kernel can stream (16-byte aligned, ld % 4 == 0,
+// V % 4 == 0, ring + bitset within shared memory).
+bool rows_tma_ok(const float* d_logits, int64_t ld, int V);
+// Argument checks of quasar_sampler_pick_batch (QUASAR_OK, QUASAR_EINVAL or
+// QUASAR_EUNSUPPORTED); B == 0 passes.
+int check_pick_batch_args(const float* d_logits, int64_t ld, int B, int V, const quasar_sample_params* d_params,
+                          const quasar_sample_params* h_params, const uint64_t* d_rng, const int32_t* d_hist,
+                          int hist_cap, const int32_t* d_hist_len, const int32_t* d_hist_head, int record,
+                          const int32_t* d_out);
 // Launches kernel A (one streaming pass per row) and kernel B (cuts and draw).
 cudaError_t launch_sample_rows(const RowsArgs& args, void* workspace, cudaStream_t stream);
 // Vocab shards: kernel A alone (per-row stats into args.shard_stats), kernel

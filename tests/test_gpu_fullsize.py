@@ -1,7 +1,8 @@
 """Full-size batches (BASELINE.json configs 3 and 5) on the GPU, checked
 through properties that do not depend on the batch size, plus oracle parity
-on an evenly spread subset of rows (their inputs regenerated on the CPU from
-the same counter-based recipe, bit for bit):
+row by row (config 3: all 4096 rows; config 5: 2048 of its 16384 rows, every
+8th), with the oracle fed the very bits the GPU sampled (the synthetic recipe
+is bit-identical on both sides, tests/test_gpu_parity.py::test_synth_bits_match):
 
 * every id is a column index; every stochastic row advanced its PRNG by
   exactly one xorshift64* step (sample.c:72-81), bit-exact;
@@ -9,7 +10,7 @@ the same counter-based recipe, bit for bit):
   overwrite the oldest entry and advance the head);
 * every row took the candidate path, kept >= 1 token, and the chosen token's
   p is at or above the min-p floor min_p * p_max (sample.c:162-167);
-* the subset matches the reference sampler under the stated tolerance."""
+* the compared rows match the reference sampler under the stated tolerance."""
 import numpy as np
 import pytest
 
@@ -55,9 +56,7 @@ def _run(kind, scale, seed, B, H, hist_seed, temps, prm, seeds):
     torch.cuda.synchronize()
     res = dict(ids=out.cpu().numpy(), diag=diag.cpu().numpy().view(q.DIAG_DTYPE).reshape(B),
                rng=rng.cpu().numpy().view(np.uint64), hist=hist.cpu().numpy(), hist0=hist0,
-               head0=head0, head1=hist_head.cpu().numpy(), len1=hist_len.cpu().numpy())
-    del logits
-    torch.cuda.empty_cache()
+               head0=head0, head1=hist_head.cpu().numpy(), len1=hist_len.cpu().numpy(), logits=logits)
     return res
 
 
@@ -76,13 +75,21 @@ def _properties(r, prm, seeds, H):
     assert (d["p_chosen"] >= floor * (1 - 1e-6)).all()
 
 
-def _subset_parity(r, kind, scale, seed, hist_seed, H, prm, seeds, step):
+def _row_parity(r, H, prm, seeds, step, chunk=512):
+    """Rows 0, step, 2*step, ... against the reference, in chunks of rows
+    copied from the sampled device matrix."""
+    import torch
     rows = np.arange(0, r["ids"].size, step)
-    logits = np.concatenate([O.synth_logits(kind, seed, int(i), 1, V_FULL, scale) for i in rows])
-    hist = r["hist0"][rows]
-    res, rng_ref = O.pick_rows(logits, prm[rows], seeds[rows], hist=hist,
-                               hist_len=np.full(rows.size, H, np.int32), hist_head=r["head0"][rows])
-    assert_parity(r["ids"][rows], r["diag"][rows], r["rng"][rows], res, rng_ref)
+    reps = []
+    for c0 in range(0, rows.size, chunk):
+        sel = rows[c0:c0 + chunk]
+        logits = r["logits"][torch.from_numpy(sel).to(r["logits"].device)].cpu().numpy()
+        res, rng_ref = O.pick_rows(logits, prm[sel], seeds[sel], hist=r["hist0"][sel],
+                                   hist_len=np.full(sel.size, H, np.int32), hist_head=r["head0"][sel])
+        reps.append(assert_parity(r["ids"][sel], r["diag"][sel], r["rng"][sel], res, rng_ref))
+    n_mis = sum(x["mismatched_near_boundary"] for x in reps)
+    assert n_mis <= 0.01 * rows.size, f"{n_mis} of {rows.size} rows differ (all near boundaries)"
+    print({"rows_compared": int(rows.size), "mismatched_near_boundary": n_mis})
 
 
 def test_config3_full_batch():
@@ -92,7 +99,7 @@ def test_config3_full_batch():
     seeds = np.arange(B, dtype=np.uint64) + np.uint64(5000)
     r = _run(O.SYNTH_NORMAL, 3.0, 3, B, H, 33, temps, prm, seeds)
     _properties(r, prm, seeds, H)
-    _subset_parity(r, O.SYNTH_NORMAL, 3.0, 3, 33, H, prm, seeds, 64)
+    _row_parity(r, H, prm, seeds, 1)
 
 
 def test_config5_full_batch():
@@ -101,4 +108,4 @@ def test_config5_full_batch():
     seeds = np.arange(B, dtype=np.uint64) + np.uint64(9000)
     r = _run(O.SYNTH_ZIPF, 1.1, 5, B, H, 55, None, prm, seeds)
     _properties(r, prm, seeds, H)
-    _subset_parity(r, O.SYNTH_ZIPF, 1.1, 5, 55, H, prm, seeds, 512)
+    _row_parity(r, H, prm, seeds, 8)
