@@ -82,11 +82,6 @@ constexpr int QMAX = 4096;                     // qualifying thread-tiles re-rea
 // a list entry is slot * CONSUMERS + thread, slot < TMAX_TILES: 16 bits hold it
 static_assert(TMAX_TILES * CONSUMERS <= 65536, "16-bit slot-list entries");
 constexpr int NB = 1024;                       // radix bins per level (10 bits)
-// Candidates of a min-p row that kernel A lists while it streams (entries
-// (scaled logit bits << 32) | id, every element above the CTA's running
-// min-p threshold): a superset of the row's min-p survivors. A row whose
-// list would exceed it is finished from the tile tables instead.
-constexpr int LIST_CAP = 2048;
 constexpr long long WAIT_CYCLES = 1ll << 32;   // ~2 s: bound on any mbarrier wait
 constexpr float REF_SLACK = 64.0f;             // kernel A: exp reference lag (nats), e^64 << FLT_MAX
 #ifndef QS_LDG_DEPTH
@@ -146,10 +141,6 @@ struct SharedA : Shared {
     // parameters and ring position; its first CONSUMERS ring slots go to tfmax
     quasar_sample_params nxt_pr;
     int nxt_len, nxt_head;
-    // candidate listing of min-p rows: the CTA's running max (ord_key) and
-    // the entries appended so far
-    unsigned int cmax;
-    int nlist;
 };
 
 // Barrier of the 256 consumer threads (warps 0-7); the TMA producer warp never
