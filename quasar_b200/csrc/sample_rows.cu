@@ -200,6 +200,9 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
 __device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
 }
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
@@ -909,6 +912,7 @@ __device__ __forceinline__ int reg_elem(int it, int tid, int j) {
 
 struct LdgSource {
     static constexpr bool kRegs = true;
+    static constexpr bool kPick = false;  // penalized values are claimed at the row's end
     float nxt[LDG_DEPTH][16];  // tiles it+1 .. it+LDG_DEPTH in flight
     __device__ __forceinline__ void begin(const Row& R) {
 #pragma unroll
@@ -940,6 +944,7 @@ struct LdgSource {
         if (it + LDG_DEPTH < R.ntiles) load(R, it + LDG_DEPTH, nxt[LDG_DEPTH - 1]);
     }
     __device__ __forceinline__ void release() {}
+    __device__ __forceinline__ uint32_t stage_addr() const { return 0u; }  // no ring (never picks up)
 };
 
 // The slow side of a ring wait: the chunk has not landed yet. Gives up at
@@ -951,8 +956,13 @@ __device__ __noinline__ bool ring_wait_slow(uint32_t bar, uint32_t par, int* abo
     return false;
 }
 
+// kPickable: stochastic rows with long histories pick their penalized values
+// up from the ring (a separate kernel instance, so the common case's code is
+// not affected by it).
+template <bool kPickable>
 struct TmaSource {
     static constexpr bool kRegs = false;
+    static constexpr bool kPick = kPickable;
     uint32_t ring_u32;  // NSTAGE tiles (shared-window address)
     uint32_t thr_off;   // 64 * tid + 16 * chunk_swz(tid)
     uint32_t full0, empty0;
@@ -985,6 +995,11 @@ struct TmaSource {
         __syncwarp();
         if ((threadIdx.x & 31) == 0) mbar_arrive(empty0 + 8u * (g % NSTAGE));
         g++;
+    }
+    // shared address of this thread's 64 bytes in the chunk last taken by
+    // get() (valid until release())
+    __device__ __forceinline__ uint32_t stage_addr() const {
+        return ring_u32 + (uint32_t)(g % NSTAGE) * TILE_BYTES + thr_off;
     }
 };
 
@@ -1066,10 +1081,23 @@ __device__ __forceinline__ void stage_next_row(const RowsArgs& a, int row, Share
     }
     cp_async_commit();
 }
+// A stochastic row whose history ring has more slots than there are consumer
+// threads: its penalized values are picked up in the stream (from the ring
+// of the bulk-copy kernel), not claimed and gathered at the row's end, where
+// the stream has already pushed those logits out of L2.
+__device__ __forceinline__ bool picks_in_stream(const RowCtx& c, const Row& R) {
+    return R.use_pen && c.P.T > 0.0f && c.cap > CONSUMERS;
+}
+
 // staged: stage_next_row ran for this row. my_id: the column id in this
 // thread's ring slot (threadIdx.x) when that slot holds an entry, else -1;
 // its logit is copied into s.tfmax[threadIdx.x] (idle in kernel A) while the
 // row streams, for claim_penalized.
+// pick_tma: the row is streamed through the bulk-copy ring, so a stochastic
+// row with a long history (more ring slots than consumer threads) picks its
+// penalized values up from the ring while it streams (pick_penalized) and
+// needs no staged logit.
+template <bool kPickTma>
 __device__ __forceinline__ RowCtx row_setup(const RowsArgs& a, int row, Row& R, uint32_t* bits, SharedA& s,
                                             int& my_id, bool staged) {
     const int tid = threadIdx.x;
@@ -1090,7 +1118,7 @@ __device__ __forceinline__ RowCtx row_setup(const RowsArgs& a, int row, Row& R, 
             const int id = (id64 >= 0 && id64 < a.V) ? (int)id64 : -1;
             if (id >= 0) {
                 atomicOr(&bits[id >> 5], 1u << (pen_bit(id) & 31));
-                if (p == tid) {
+                if (p == tid && !(kPickTma && picks_in_stream(c, R))) {
                     my_id = id;
                     cp_async4(smem_u32(&s.tfmax[tid]), R.ptr + id);
                 }
@@ -1151,7 +1179,9 @@ __device__ __forceinline__ void row_finish(const RowsArgs& a, int row, const Row
 // alternate, the next tile's loads in flight while one is processed, with
 // unchecked 256-bit loads for every tile but the last. Ring: tiles come from
 // shared memory and the stage is released as soon as it is in registers.
-template <class Src, class F>
+// kBodyReleases: the body releases each ring chunk itself (after reading
+// more of it than the registers get() filled).
+template <bool kBodyReleases = false, class Src, class F>
 __device__ __forceinline__ void stream_tiles(const Row& R, Src& src, Shared& s, F& body) {
     if constexpr (Src::kRegs) {
         float va[16], vb[16];
@@ -1167,12 +1197,12 @@ __device__ __forceinline__ void stream_tiles(const Row& R, Src& src, Shared& s, 
         for (int it = 0; it + 1 < R.ntiles; it++) {
             float v[16];
             src.template get<false>(R, it, v, s);
-            src.release();
+            if constexpr (!kBodyReleases) src.release();
             body(v, it, std::false_type());
         }
         float v[16];
         src.template get<true>(R, R.ntiles - 1, v, s);
-        src.release();
+        if constexpr (!kBodyReleases) src.release();
         body(v, R.ntiles - 1, std::true_type());
     }
 }
@@ -1196,6 +1226,52 @@ __device__ __forceinline__ void mask_penalized(const Row& R, const uint8_t* bits
             const f32x2 hi = add2(pack2(v[4 * k + 2], v[4 * k + 3]), pack2(q[k].z, q[k].w));
             unpack2(lo, v[4 * k], v[4 * k + 1]);
             unpack2(hi, v[4 * k + 2], v[4 * k + 3]);
+        }
+    }
+}
+
+// mask_penalized plus the pick-up of the penalized values (sample.c:118-128)
+// from the ring chunk the tile came from (`stage`: this thread's 64 bytes,
+// chunk k of register chunk k at stage ^ 16k, see TmaSource::get): each
+// penalized element is penalized exactly (IEEE divide / multiply), scaled,
+// joins the thread's running max m and sum S (against m_ref, as the streamed
+// terms do) and is listed with its scaled value for kernel B. The thread's
+// 16 bitset bits are cleared once read, so the bitset is all zero at the
+// row's end. Every column is streamed once, so every distinct history id is
+// picked up once.
+template <bool kCheck>
+__device__ __forceinline__ void pick_penalized(const Row& R, uint8_t* bits8, const float4* lut, float* v, int it,
+                                               uint32_t stage, int2* pen, int* npen, float& m, float& m_ref,
+                                               double& S) {
+    const int o0 = it * OCT_TILE + 2 * (int)threadIdx.x;
+    const uint32_t mb = (!kCheck || o0 < R.noct) ? *reinterpret_cast<const uint16_t*>(bits8 + o0) : 0u;
+    if (__any_sync(FULL, mb != 0u)) {
+        const float4 q[4] = {lut[mb & 15u], lut[(mb >> 4) & 15u], lut[(mb >> 8) & 15u], lut[mb >> 12]};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const f32x2 lo = add2(pack2(v[4 * k], v[4 * k + 1]), pack2(q[k].x, q[k].y));
+            const f32x2 hi = add2(pack2(v[4 * k + 2], v[4 * k + 3]), pack2(q[k].z, q[k].w));
+            unpack2(lo, v[4 * k], v[4 * k + 1]);
+            unpack2(hi, v[4 * k + 2], v[4 * k + 3]);
+        }
+        if (mb) {
+            *reinterpret_cast<uint16_t*>(bits8 + o0) = 0;
+            uint32_t b = mb;
+            do {
+                const int j = __ffs(b) - 1;
+                b &= b - 1u;
+                float x;
+                asm volatile("ld.shared.f32 %0, [%1];" : "=f"(x) : "r"((stage ^ (16u * (uint32_t)(j >> 2))) + 4u * (uint32_t)(j & 3)));
+                const float sc = __fmul_rn(penalize(x, R.rp), R.inv_t);
+                pen[atomicAdd(npen, 1)] = make_int2(reg_elem(it, (int)threadIdx.x, j), __float_as_int(sc));
+                m = fmaxf(m, sc);
+                if (sc > m_ref + REF_SLACK) {
+                    S = S * exp((double)m_ref - (double)sc) + 1.0;
+                    m_ref = sc;
+                } else if (sc > -INFINITY) {
+                    S += (double)exp_fast(__fsub_rn(sc, m_ref));  // like the streamed terms
+                }
+            } while (b);
         }
     }
 }
@@ -1267,7 +1343,8 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
     const uint8_t* bits8 = reinterpret_cast<const uint8_t*>(bits);
     Row R;
     int my_id;
-    const RowCtx c = row_setup(a, row, R, bits, s, my_id, staged);
+    const RowCtx c = row_setup<Src::kPick>(a, row, R, bits, s, my_id, staged);
+    const bool pick = Src::kPick && picks_in_stream(c, R);
     const RowParams& P = c.P;
     src.begin(R);
 
@@ -1363,12 +1440,20 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
     // g1: one tile per table slot (compile-time); last: std::true_type when
     // `it` may be the row's last tile
     // pen: the row has penalized ids (compile-time, like g1)
+    // pen: 0 no penalized ids, 1 masked in the stream and claimed at the
+    // row's end, 2 masked and picked up in the stream (ring kernel only)
     auto run = [&](auto g1, auto pen) {
         constexpr bool kG1 = decltype(g1)::value;
-        constexpr bool kPen = decltype(pen)::value;
+        constexpr bool kPen = decltype(pen)::value == 1;
+        constexpr bool kPick = decltype(pen)::value == 2;
         auto body = [&](float (&v)[16], int it, auto last) {
             constexpr bool kMaybeLast = decltype(last)::value;
             if constexpr (kPen) mask_penalized<kMaybeLast>(R, bits8, s.pen_lut, v, it);
+            if constexpr (kPick) {
+                pick_penalized<kMaybeLast>(R, reinterpret_cast<uint8_t*>(bits), s.pen_lut, v, it, src.stage_addr(),
+                                           a.work_pen + (int64_t)row * a.hist_cap, &s.npen, m, m_ref, S);
+                src.release();
+            }
             // sample.c:142: sc = l * inv_t, rounded exactly like the reference
             // (packed pairs: each lane is the same IEEE multiply)
             f32x2 sc2[8];
@@ -1442,16 +1527,21 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
                 }
             }
         };
-        stream_tiles(R, src, s, body);
+        stream_tiles<kPick>(R, src, s, body);
     };
+    using P0 = std::integral_constant<int, 0>;
+    using P1 = std::integral_constant<int, 1>;
+    using P2 = std::integral_constant<int, Src::kPick ? 2 : 1>;  // (pick is false without a pickable ring)
     if (g == 1) {
-        if (R.use_pen) run(std::true_type(), std::true_type());
-        else run(std::true_type(), std::false_type());
+        if (pick) run(std::true_type(), P2());
+        else if (R.use_pen) run(std::true_type(), P1());
+        else run(std::true_type(), P0());
     } else {
-        if (R.use_pen) run(std::false_type(), std::true_type());
-        else run(std::false_type(), std::false_type());
+        if (pick) run(std::false_type(), P2());
+        else if (R.use_pen) run(std::false_type(), P1());
+        else run(std::false_type(), P0());
     }
-    if (R.use_pen) {
+    if (R.use_pen && !pick) {
         csync();
         // the penalized elements join the running max and sum exactly, and
         // are listed for kernel B
@@ -1516,6 +1606,9 @@ __device__ __forceinline__ void shard_norm(const RowsArgs& a, int row, float& M,
     inv = __double2float_rn(1.0 / S);
 }
 
+// kLongPen: histories longer than CONSUMERS slots (a separate kernel
+// instance: the penalized list is staged in shared memory).
+template <bool kLongPen>
 __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t* buf, uint32_t* bits,
                                            Buckets* bk, uint16_t* qlist, Shared& s) {
     const int tid = threadIdx.x, lane = tid & 31;
@@ -1566,13 +1659,23 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
     // (an aborted kernel A leaves stale summaries: keep every index in range)
     const int npen = min(max(__float_as_int(info.z), 0), a.hist_cap);
     R.use_pen = npen > 0;
+    // A list longer than one entry per thread is read twice below: it is
+    // copied once into the bottom of buf (asynchronous copies, all in flight
+    // together), where the candidates appended from the top never reach it.
+    const bool pen_staged = kLongPen && npen > CONSUMERS;
+    const int2* pen_s = reinterpret_cast<const int2*>(buf);
+    if (pen_staged) {
+        for (int i = tid; i < npen; i += CONSUMERS) cp_async8(smem_u32(buf + i), pen + i);
+        cp_async_commit();
+    }
     s.tfmax[tid] = m;
     if (tid == 0) s.ncand = 0;
-    csync();  // the bitset is clear
+    if (pen_staged) cp_async_wait_all();
+    csync();  // the bitset is clear (and the staged list has landed)
     // bitset of the penalized ids: re-reads leave them out, the select path
     // penalizes them (both come after barriers below)
     for (int i = tid; i < npen; i += CONSUMERS) {
-        const int id = (i == tid ? pen0 : pen[i]).x;
+        const int id = (pen_staged ? pen_s[i] : (i == tid ? pen0 : pen[i])).x;
         if (id >= 0 && id < R.V) atomicOr(&bits[id >> 5], 1u << (id & 31));
     }
 
@@ -1645,11 +1748,13 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
         for (; qmask; qmask &= qmask - 1ull, off++)
             if (off < QMAX) qlist[off] = (uint16_t)((__ffsll((long long)qmask) - 1) * CONSUMERS + tid);
         const int nq = min(nq_all, QMAX);
-        const int room = CAP;  // the list has its own area: every candidate entry is free
+        // the slot list has its own area: every candidate entry above a
+        // staged penalized list is free
+        const int room = pen_staged ? CAP - npen : CAP;
         // raw survivors are appended from the top of buf downwards: first the
         // penalized ids that clear the threshold
         for (int i = tid; i < npen; i += CONSUMERS) {
-            const int2 pe = i == tid ? pen0 : pen[i];
+            const int2 pe = pen_staged ? pen_s[i] : (i == tid ? pen0 : pen[i]);
             const float sc = __int_as_float(pe.y);
             if (sc >= lo && pe.x >= 0 && pe.x < R.V) {
                 const int pos = atomicAdd(&s.ncand, 1);
@@ -1802,6 +1907,7 @@ __global__ void __launch_bounds__(CONSUMERS, QS_A_CTAS) sample_rows_ldg(RowsArgs
     for (int row = blockIdx.x; row < a.B; row += gridDim.x) stream_row(a, row, src, bits, anc_s, s, row != (int)blockIdx.x);
 }
 
+template <bool kPickable>
 __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a) {
     extern __shared__ __align__(128) unsigned char dyn[];
     // the ring starts on a 64-byte boundary (the chunk swizzle flips address
@@ -1850,7 +1956,7 @@ __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a)
         }
         return;
     }
-    TmaSource src;
+    TmaSource<kPickable> src;
     src.ring_u32 = smem_u32(ring);
     src.thr_off = 64u * threadIdx.x + 16u * chunk_swz(threadIdx.x);
     src.full0 = full0;
@@ -1869,6 +1975,7 @@ __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a)
     }
 }
 
+template <bool kLongPen>
 __global__ void __launch_bounds__(CONSUMERS, 3) sample_rows_finish(RowsArgs a) {
     extern __shared__ __align__(128) unsigned char dyn[];
     uint64_t* buf = reinterpret_cast<uint64_t*>(dyn);
@@ -1876,7 +1983,7 @@ __global__ void __launch_bounds__(CONSUMERS, 3) sample_rows_finish(RowsArgs a) {
     Buckets* bk = reinterpret_cast<Buckets*>(dyn + FINISH_SCRATCH + (((size_t)a.nwords * 4 + 15) & ~(size_t)15));
     __shared__ Shared s;
     uint16_t* qlist = reinterpret_cast<uint16_t*>(reinterpret_cast<unsigned char*>(bk) + sizeof(Buckets));
-    if ((int)blockIdx.x < a.B) finish_row(a, blockIdx.x, buf, bits, bk, qlist, s);  // one row per CTA
+    if ((int)blockIdx.x < a.B) finish_row<kLongPen>(a, blockIdx.x, buf, bits, bk, qlist, s);  // one row per CTA
 }
 
 // Merge of the vocab shards' candidates, one CTA per row: the G*k gathered
@@ -1963,7 +2070,7 @@ struct KernelCfg {
     std::atomic<size_t> smem_set[64];
     std::atomic<int> grid[64];  // resident CTAs of the kernel on each device
 };
-KernelCfg g_ldg, g_tma, g_fin, g_merge;
+KernelCfg g_ldg, g_tma, g_tma_pick, g_fin, g_fin_long, g_merge;
 std::mutex g_cfg_mu;
 
 cudaError_t configure(KernelCfg& cfg, const void* fn, int threads, size_t smem, int dev, int& grid) {
@@ -2024,9 +2131,15 @@ cudaError_t launch_stream(const RowsArgs& a, int dev, cudaStream_t stream) {
     if (a.tma) {
         const size_t smem = rows_tma_smem_bytes(a.V);
         int grid = 0;
-        err = configure(g_tma, (const void*)rows::sample_rows_tma, rows::CONSUMERS + 32, smem, dev, grid);
-        if (err != cudaSuccess) return err;
-        rows::sample_rows_tma<<<min(a.B, grid), rows::CONSUMERS + 32, smem, stream>>>(a);
+        if (a.hist && a.hist_cap > rows::CONSUMERS) {  // long histories: penalized values picked up in the stream
+            err = configure(g_tma_pick, (const void*)rows::sample_rows_tma<true>, rows::CONSUMERS + 32, smem, dev, grid);
+            if (err != cudaSuccess) return err;
+            rows::sample_rows_tma<true><<<min(a.B, grid), rows::CONSUMERS + 32, smem, stream>>>(a);
+        } else {
+            err = configure(g_tma, (const void*)rows::sample_rows_tma<false>, rows::CONSUMERS + 32, smem, dev, grid);
+            if (err != cudaSuccess) return err;
+            rows::sample_rows_tma<false><<<min(a.B, grid), rows::CONSUMERS + 32, smem, stream>>>(a);
+        }
     } else {
         const size_t smem = rows_smem_bytes(a.V);
         int grid = 0;
@@ -2041,9 +2154,17 @@ cudaError_t launch_stream(const RowsArgs& a, int dev, cudaStream_t stream) {
 cudaError_t launch_finish(const RowsArgs& a, int dev, cudaStream_t stream) {
     const size_t fsmem = rows_finish_smem_bytes(a.V);
     int grid = 0;  // unused: one CTA per row
-    cudaError_t err = configure(g_fin, (const void*)rows::sample_rows_finish, rows::CONSUMERS, fsmem, dev, grid);
-    if (err != cudaSuccess) return err;
-    rows::sample_rows_finish<<<a.B, rows::CONSUMERS, fsmem, stream>>>(a);
+    if (a.hist && a.hist_cap > rows::CONSUMERS) {
+        cudaError_t err =
+            configure(g_fin_long, (const void*)rows::sample_rows_finish<true>, rows::CONSUMERS, fsmem, dev, grid);
+        if (err != cudaSuccess) return err;
+        rows::sample_rows_finish<true><<<a.B, rows::CONSUMERS, fsmem, stream>>>(a);
+    } else {
+        cudaError_t err =
+            configure(g_fin, (const void*)rows::sample_rows_finish<false>, rows::CONSUMERS, fsmem, dev, grid);
+        if (err != cudaSuccess) return err;
+        rows::sample_rows_finish<false><<<a.B, rows::CONSUMERS, fsmem, stream>>>(a);
+    }
     return cudaGetLastError();
 }
 }  // namespace
