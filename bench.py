@@ -338,8 +338,9 @@ def run_vocab_sharded(args) -> None:
 
     Every rank holds V/N columns of the same 8192 rows (N(0,3), seeded);
     top_k 40, top_p 0.9, temperature 0.8, no history. One step = one
-    VocabShardedSampler.pick: per-shard stats, an NCCL all-gather, per-shard
-    top-40 candidates, a second all-gather, merge/cut/draw on every rank.
+    quasar_shard_pick call (NcclShardedSampler.pick): per-shard stats, an
+    NCCL all-gather, per-shard top-40 candidates, a second all-gather,
+    merge/cut/draw on every rank.
     `value` = rows per second of the whole job (all ranks sample the same
     rows together); the roofline counts each rank's shard bytes against one
     GPU's measured bandwidth."""
@@ -366,7 +367,12 @@ def run_vocab_sharded(args) -> None:
     seeds = np.arange(rows, dtype=np.uint64) + np.uint64(SEED_RNG)
     rng = torch.from_numpy(seeds.view(np.int64).copy()).to(dev)
     out = torch.empty(rows, dtype=torch.int32, device=dev)
-    smp = q.VocabShardedSampler(K)
+    # the C entry (quasar_shard_pick) over the library's own NCCL communicator;
+    # torch.distributed only hands out its id and times the step
+    uid = [q.NcclCommunicator.unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    comm = q.NcclCommunicator(world, rank, uid[0], timeout_ms=60000)
+    smp = q.NcclShardedSampler(comm, K)
     prm = {"temperature": 0.8, "top_k": K, "top_p": 0.9}
     stream = torch.cuda.current_stream(dev)
 
@@ -394,6 +400,23 @@ def run_vocab_sharded(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
     clk = clocks.stop() if rank == 0 else None
+    comm.wait(stream, timeout_ms=60000)
+    # where a step's device time goes: one traced step (CUPTI through
+    # torch.profiler), device time per kernel, the NCCL all-gathers included
+    phases = None
+    if args.trace_phases:
+        from torch.profiler import ProfilerActivity, profile
+        dist.barrier()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            for _ in range(3):
+                step()
+            torch.cuda.synchronize(dev)
+        phases = {}
+        for ev in prof.key_averages():
+            dt = getattr(ev, "device_time_total", None) or getattr(ev, "cuda_time_total", 0)
+            if dt and ev.count:
+                phases[ev.key[:80]] = round(dt / 3.0, 2)  # us per step
+        dist.barrier()
     per_step = ms / 1e3 / args.steps
     shard_bytes = rows * (vs * 4 + 24)
     peak, peak_kind = peak_hbm()
@@ -406,10 +429,15 @@ def run_vocab_sharded(args) -> None:
             "roofline": {"bound": "hbm", "achieved": shard_bytes / per_step / 1e9, "peak": peak, "unit": "GB/s",
                          "frac": shard_bytes / per_step / 1e9 / peak, "traffic": None, "peak_source": peak_kind,
                          "algorithmic_bytes_per_launch": shard_bytes},
-            "gpu_launches": args.steps * 3, "clocks": clk}
+            "gpu_launches": args.steps * 3, "clocks": clk,
+            "exchange": "quasar_shard_pick: two in-place NCCL all-gathers (libquasar_cuda communicator, "
+                        "non-blocking, 60 s limit)"}
+    if phases is not None:
+        line["phases_us_per_step_rank0"] = phases
     if rank == 0:
         print(json.dumps(line), flush=True)
     dist.barrier()
+    comm.close()
     dist.destroy_process_group()
 
 
@@ -426,6 +454,8 @@ def main() -> None:
                                                           "runs use fewer)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg (profiling)")
     ap.add_argument("--flags", type=int, default=0, help="quasar_sampler_pick_batch flags (A/B runs)")
+    ap.add_argument("--trace-phases", action="store_true",
+                    help="vocab mode: trace one step per kernel (torch.profiler / CUPTI) after the timed region")
     ap.add_argument("--mode", default="rows", choices=["rows", "vocab"],
                     help="rows: config 3, rows split over GPUs (default); vocab: config 4, vocab split")
     args = ap.parse_args()

@@ -200,9 +200,13 @@ int quasar_sampler_pick_batch_noalloc(const float *d_logits, int64_t ld, int B, 
  *   2. quasar_shard_candidates -> d_cand[B][k] per rank; all-gather -> [G][B][k]
  *   3. quasar_shard_finish     -> ids, PRNG steps, ring appends (every rank)
  * Stochastic rows need 1 <= top_k <= k <= 256 (the merge is exact because
- * the global top-k lies in the union of the shards' top-k); other stochastic
- * rows, and rows whose candidates a shard cannot bound, come back as -1.
- * Greedy rows merge the shards' penalized argmax (lowest global id on ties). */
+ * the global top-k lies in the union of the shards' top-k), or min_p > 0
+ * with at most k keys per shard at or above the min-p threshold of the
+ * global max (every survivor of the floor is sent, so the top-p and min-p
+ * cuts over the merged keys are exact); other stochastic rows (top-p alone,
+ * pure multinomial), and rows whose candidates a shard cannot bound or send,
+ * come back as -1. Greedy rows merge the shards' penalized argmax (lowest
+ * global id on ties). */
 typedef struct {
     float   max;   /* stochastic row: max scaled logit of the shard;
                       greedy row: its largest penalized logit */
@@ -244,6 +248,76 @@ int quasar_shard_finish(const uint64_t *d_all_cand, const quasar_shard_stat *d_a
                         int32_t *d_hist_len, int32_t *d_hist_head,
                         int record,
                         int32_t *d_out, quasar_pick_diag *d_diag, void *stream);
+
+/* ---- vocab-sharded sampling over NCCL (no counterpart in the reference) ----
+ * The three phases above with their two exchanges, in one call on the
+ * caller's stream, for callers in C. NCCL is loaded at run time: the
+ * libnccl.so.2 the process already has, else the file QUASAR_NCCL_LIBRARY
+ * names, else libnccl.so.2 from the loader path (QUASAR_ENCCL when none
+ * loads). Communicators made by quasar_nccl_init are non-blocking: every
+ * NCCL call is followed until it has left the host, under the communicator's
+ * time limit; on an error or on expiry the communicator is aborted
+ * (ncclCommAbort) and the call returns QUASAR_ENCCL - a rank that never joins
+ * or stops answering ends the others' calls instead of hanging them. An
+ * aborted communicator stays unusable (every later call: QUASAR_ENCCL). */
+#define QUASAR_NCCL_ID_BYTES 128   /* sizeof(ncclUniqueId) */
+typedef struct quasar_nccl quasar_nccl;
+
+/* QUASAR_OK when an NCCL library could be loaded, else QUASAR_ENCCL. */
+int quasar_nccl_available(void);
+
+/* A new communicator id (rank 0 makes it; every rank passes it to _init). */
+int quasar_nccl_unique_id(void *id_out /* QUASAR_NCCL_ID_BYTES */);
+
+/* Rank `rank` of `nranks` joins the communicator of unique_id on the current
+ * CUDA device. timeout_ms bounds the join and every later NCCL call of this
+ * communicator (0: no limit). */
+int quasar_nccl_init(quasar_nccl **comm, int nranks, int rank, const void *unique_id, int timeout_ms);
+
+/* Wraps a communicator the caller made (an ncclComm_t of the same NCCL
+ * library, on the current device); quasar_nccl_free does not destroy it. */
+int quasar_nccl_wrap(quasar_nccl **comm, void *nccl_comm, int nranks, int rank, int timeout_ms);
+
+/* Aborts the communicator (ncclCommAbort): its operations still queued or
+ * running end; it cannot be used again. */
+int quasar_nccl_abort(quasar_nccl *comm);
+
+/* Finalizes and destroys a communicator made by quasar_nccl_init (bounded by
+ * its time limit), and frees the handle. NULL-safe. */
+int quasar_nccl_free(quasar_nccl *comm);
+
+/* Blocks until the work queued on `stream` so far has completed, while
+ * watching the communicator: an NCCL error, or timeout_ms (> 0) passing
+ * first, aborts it and returns QUASAR_ENCCL (its kernels still waiting for a
+ * peer then end). */
+int quasar_nccl_wait(quasar_nccl *comm, void *stream, int timeout_ms);
+
+/* Workspace of quasar_shard_pick: the row summaries of
+ * quasar_sampler_workspace_bytes(B, hist_cap) plus the gathered stats
+ * [G][B] and candidate keys [G][B][k]. */
+size_t quasar_shard_workspace_bytes(int B, int hist_cap, int G, int k);
+
+/* Samples B rows split by vocab over the communicator's ranks: this rank
+ * holds global columns [col0, col0 + Vs) of each row (d_logits, row stride
+ * ld); every rank passes its replica of the per-row parameters, PRNG states
+ * and history rings, and every rank ends with the same ids, states and rings
+ * (quasar_shard_stats -> all-gather -> quasar_shard_candidates ->
+ * all-gather -> quasar_shard_finish, the gathers in place in d_workspace,
+ * 256-byte aligned, quasar_shard_workspace_bytes(B, hist_cap, G, k) bytes).
+ * Row requirements as for the phases (stochastic rows: 1 <= top_k <= k, or
+ * min_p > 0 with at most k survivors of the min-p floor per shard; other rows
+ * come back as -1). Asynchronous on `stream`; pair with quasar_nccl_wait to
+ * bound the wait for the peers. */
+int quasar_shard_pick(quasar_nccl *comm, const float *d_logits, int64_t ld, int B, int Vs, int64_t col0,
+                      const quasar_sample_params *d_params,
+                      const quasar_sample_params *h_params,
+                      uint64_t *d_rng,
+                      int32_t *d_hist, int hist_cap,
+                      int32_t *d_hist_len, int32_t *d_hist_head,
+                      int record,
+                      int32_t *d_out, quasar_pick_diag *d_diag,
+                      int k, void *d_workspace, size_t workspace_bytes,
+                      int flags, void *stream);
 
 /* ---- synthetic inputs (benchmark / test utility, not in the reference) ---- */
 

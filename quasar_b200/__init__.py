@@ -8,7 +8,7 @@ from ._lib import (FLAG_EXACT_SELECT, PATH_CANDIDATE, PATH_GREEDY, PATH_SELECT, 
                    SYNTH_GUMBEL_PEAK, SYNTH_NORMAL, SYNTH_ZIPF, LIB_PATH, QuasarError, lib)
 from .sampler import (DIAG_DTYPE, PARAMS_DTYPE, Sampler, SampleParams, make_params, params_to_device,
                       pick_batch, synth_hist, synth_logits, synth_uniform, workspace_bytes)
-from .sharded import VocabShardedSampler
+from .sharded import NcclCommunicator, NcclShardedSampler, VocabShardedSampler
 
 lib()  # fail loudly at import when the CUDA library is missing
 
@@ -16,4 +16,4 @@ __all__ = ["Sampler", "SampleParams", "make_params", "params_to_device", "pick_b
            "synth_logits", "synth_hist", "synth_uniform", "PARAMS_DTYPE", "DIAG_DTYPE",
            "FLAG_EXACT_SELECT", "PATH_GREEDY", "PATH_CANDIDATE", "PATH_SELECT",
            "SYNTH_NORMAL", "SYNTH_GUMBEL_PEAK", "SYNTH_ZIPF", "LIB_PATH", "QuasarError", "lib",
-           "QUASAR_NOALLOC_WORKSPACE_BYTES", "VocabShardedSampler"]
+           "QUASAR_NOALLOC_WORKSPACE_BYTES", "VocabShardedSampler", "NcclCommunicator", "NcclShardedSampler"]

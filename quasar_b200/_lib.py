@@ -46,6 +46,16 @@ SIGNATURES = {
     "quasar_shard_candidates": ([_P, _I64, _I, _I, _I64, _P, _P, _P, _I, _P, _P, _P, _I, _I, _I, _P, _P,
                                  ctypes.c_size_t, _I, _P], _I),
     "quasar_shard_finish": ([_P, _P, _I, _I, _I, _P, _P, _P, _P, _I, _P, _P, _I, _P, _P, _P], _I),
+    "quasar_nccl_available": ([], _I),
+    "quasar_nccl_unique_id": ([_P], _I),
+    "quasar_nccl_init": ([_P, _I, _I, _P, _I], _I),
+    "quasar_nccl_wrap": ([_P, _P, _I, _I, _I], _I),
+    "quasar_nccl_abort": ([_P], _I),
+    "quasar_nccl_free": ([_P], _I),
+    "quasar_nccl_wait": ([_P, _P, _I], _I),
+    "quasar_shard_workspace_bytes": ([_I, _I, _I, _I], ctypes.c_size_t),
+    "quasar_shard_pick": ([_P, _P, _I64, _I, _I, _I64, _P, _P, _P, _P, _I, _P, _P, _I, _P, _P, _I, _P,
+                           ctypes.c_size_t, _I, _P], _I),
     "quasar_synth_logits": ([_I, _U64, _I64, _I, _I, _I64, _F, _P, _P], _I),
     "quasar_synth_hist": ([_U64, _I64, _I, _I, _I, _P, _P], _I),
     "quasar_synth_uniform": ([_U64, _I64, _I, _F, _F, _P, _P], _I),

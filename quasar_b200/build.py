@@ -22,7 +22,7 @@ INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I" + INCLUDE]
 PER_FILE = {"synth.cu": ["-fmad=false"]}
-LINK_LIBS: list[str] = []
+LINK_LIBS: list[str] = ["-ldl"]  # NCCL is dlopen'ed at run time (nccl_shard.cu), not linked
 
 
 def nvcc() -> str:

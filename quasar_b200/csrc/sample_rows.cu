@@ -82,6 +82,9 @@ constexpr int QMAX = 4096;                     // qualifying thread-tiles re-rea
 // a list entry is slot * CONSUMERS + thread, slot < TMAX_TILES: 16 bits hold it
 static_assert(TMAX_TILES * CONSUMERS <= 65536, "16-bit slot-list entries");
 constexpr int NB = 1024;                       // radix bins per level (10 bits)
+// Candidate key a vocab shard sends first when it has more min-p survivors
+// than keys to send (no real key reaches it: p keys are at most 1.0f's bits)
+constexpr uint64_t SHARD_OVERFLOW = ~0ull;
 constexpr long long WAIT_CYCLES = 1ll << 32;   // ~2 s: bound on any mbarrier wait
 constexpr float REF_SLACK = 64.0f;             // kernel A: exp reference lag (nats), e^64 << FLT_MAX
 #ifndef QS_LDG_DEPTH
@@ -1608,7 +1611,9 @@ __device__ __forceinline__ void shard_norm(const RowsArgs& a, int row, float& M,
 
 // kLongPen: histories longer than CONSUMERS slots (a separate kernel
 // instance: the penalized list is staged in shared memory).
-template <bool kLongPen>
+// kShard: the candidate kernel of a vocab shard (quasar_shard_candidates),
+// also an instance of its own.
+template <bool kLongPen, bool kShard>
 __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t* buf, uint32_t* bits,
                                            Buckets* bk, uint16_t* qlist, Shared& s) {
     const int tid = threadIdx.x, lane = tid & 31;
@@ -1637,7 +1642,7 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
     uint64_t st_rng = a.rng ? a.rng[row] : 0ull;
     // kernel A's abort word (read where the row is written)
     const int aborted = tid == 0 ? *reinterpret_cast<volatile int*>(a.work_abort) : 0;
-    const bool shard = a.shard_cand != nullptr;  // a vocab shard: emit candidates, no draw
+    constexpr bool shard = kShard;  // a vocab shard: emit candidates, no draw
     uint64_t* cand = shard ? a.shard_cand + (int64_t)row * a.shard_k : nullptr;
     if (!(pr.temperature > 0.0f)) {
         // greedy: finished by kernel A; a shard contributes its best column
@@ -1685,7 +1690,12 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
     const bool by_minp = P.min_p > 0.0f;
     const bool by_topk = P.top_k > 0 && P.top_k <= TOPK_MAX;
     // (a shard emits k candidates per row: its rows need 1 <= top_k <= k)
-    if (!(a.flags & QUASAR_FLAG_EXACT_SELECT) && (by_minp || by_topk) && (!shard || (by_topk && P.top_k <= a.shard_k))) {
+    // A vocab shard can stand for its part of a row when its k best keys
+    // cover the row's top_k (top_k <= k), or when it sends every key at or
+    // above the min-p threshold of the global max (at most k of them: more
+    // are reported as an overflow, see below).
+    const bool shard_topk = by_topk && P.top_k <= a.shard_k;
+    if (!(a.flags & QUASAR_FLAG_EXACT_SELECT) && (by_minp || by_topk) && (!shard || shard_topk || by_minp)) {
         float tau = -INFINITY;
         // (logf is within a few ulp: far inside the 0.01 margin)
         if (by_minp) tau = __fadd_rn(R.M, logf(fminf(P.min_p, 1.0f)) - 0.01f);
@@ -1829,7 +1839,12 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
         }
         csync();
         const int nk = nq_all <= QMAX ? s.ncand : CAP + 1;
-        if (nk > 0 && nk <= RANK_MAX) {
+        if (shard && !shard_topk && nk > a.shard_k) {
+            // a min-p row with more survivors in this shard than it may send:
+            // the all-ones key tells the merge (the row then gets id -1)
+            for (int i = tid; i < a.shard_k; i += CONSUMERS) cand[i] = i == 0 ? SHARD_OVERFLOW : 0ull;
+            done = true;
+        } else if (nk > 0 && nk <= RANK_MAX) {
             rank_cuts(buf, nk, R, P, by_minp ? __fmul_rn(P.min_p, R.inv) : 0.0f, u, s, cand, a.shard_k, a.col0);
             done = true;
             path = QUASAR_PATH_CANDIDATE;
@@ -1975,7 +1990,7 @@ __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a)
     }
 }
 
-template <bool kLongPen>
+template <bool kLongPen, bool kShard>
 __global__ void __launch_bounds__(CONSUMERS, 3) sample_rows_finish(RowsArgs a) {
     extern __shared__ __align__(128) unsigned char dyn[];
     uint64_t* buf = reinterpret_cast<uint64_t*>(dyn);
@@ -1983,7 +1998,7 @@ __global__ void __launch_bounds__(CONSUMERS, 3) sample_rows_finish(RowsArgs a) {
     Buckets* bk = reinterpret_cast<Buckets*>(dyn + FINISH_SCRATCH + (((size_t)a.nwords * 4 + 15) & ~(size_t)15));
     __shared__ Shared s;
     uint16_t* qlist = reinterpret_cast<uint16_t*>(reinterpret_cast<unsigned char*>(bk) + sizeof(Buckets));
-    if ((int)blockIdx.x < a.B) finish_row<kLongPen>(a, blockIdx.x, buf, bits, bk, qlist, s);  // one row per CTA
+    if ((int)blockIdx.x < a.B) finish_row<kLongPen, kShard>(a, blockIdx.x, buf, bits, bk, qlist, s);  // one row per CTA
 }
 
 // Merge of the vocab shards' candidates, one CTA per row: the G*k gathered
@@ -2012,6 +2027,8 @@ __global__ void __launch_bounds__(CONSUMERS, 3) sample_rows_merge(RowsArgs a) {
         int cnt = 0;
         for (int i = tid; i < n; i += CONSUMERS) cnt += (buf[i] >> 32) != 0ull ? 1 : 0;
         const int nk = block_sum_i(cnt, s);  // real keys sort first
+        // a shard that overflowed its min-p keys (the largest key sorts first)
+        const bool overflow = nk > 0 && buf[0] == SHARD_OVERFLOW;
         if (!(pr.temperature > 0.0f)) {
             if (tid == 0)
                 write_row(a, row, c, nk > 0 ? (int)(~(uint32_t)buf[0]) : 0, 0, 1.0f, 0.0f, QUASAR_PATH_GREEDY, 0ull);
@@ -2020,10 +2037,10 @@ __global__ void __launch_bounds__(CONSUMERS, 3) sample_rows_merge(RowsArgs a) {
             shard_norm(a, row, M, inv);
             uint64_t st_rng = a.rng[row];
             const double u = rng_unit(&st_rng);  // sample.c:173
-            if (nk > 0) {
+            if (nk > 0 && !overflow) {
                 candidate_cuts(buf, nk, c.P, c.P.min_p > 0.0f ? __fmul_rn(c.P.min_p, inv) : 0.0f, u, s);
             } else if (tid == 0) {
-                s.res_id = -1;  // a shard could not bound its candidates
+                s.res_id = -1;  // a shard could not bound (or send) its candidates
                 s.res_nc = 0;
                 s.res_p = 0.0f;
             }
@@ -2070,7 +2087,7 @@ struct KernelCfg {
     std::atomic<size_t> smem_set[64];
     std::atomic<int> grid[64];  // resident CTAs of the kernel on each device
 };
-KernelCfg g_ldg, g_tma, g_tma_pick, g_fin, g_fin_long, g_merge;
+KernelCfg g_ldg, g_tma, g_tma_pick, g_fin, g_fin_long, g_fin_shard, g_fin_shard_long, g_merge;
 std::mutex g_cfg_mu;
 
 cudaError_t configure(KernelCfg& cfg, const void* fn, int threads, size_t smem, int dev, int& grid) {
@@ -2154,17 +2171,19 @@ cudaError_t launch_stream(const RowsArgs& a, int dev, cudaStream_t stream) {
 cudaError_t launch_finish(const RowsArgs& a, int dev, cudaStream_t stream) {
     const size_t fsmem = rows_finish_smem_bytes(a.V);
     int grid = 0;  // unused: one CTA per row
-    if (a.hist && a.hist_cap > rows::CONSUMERS) {
-        cudaError_t err =
-            configure(g_fin_long, (const void*)rows::sample_rows_finish<true>, rows::CONSUMERS, fsmem, dev, grid);
-        if (err != cudaSuccess) return err;
-        rows::sample_rows_finish<true><<<a.B, rows::CONSUMERS, fsmem, stream>>>(a);
-    } else {
-        cudaError_t err =
-            configure(g_fin, (const void*)rows::sample_rows_finish<false>, rows::CONSUMERS, fsmem, dev, grid);
-        if (err != cudaSuccess) return err;
-        rows::sample_rows_finish<false><<<a.B, rows::CONSUMERS, fsmem, stream>>>(a);
-    }
+    const bool long_pen = a.hist && a.hist_cap > rows::CONSUMERS;
+    const bool shard = a.shard_cand != nullptr;
+    // one instance per (long history, vocab shard) combination
+    const void* fn = shard ? (long_pen ? (const void*)rows::sample_rows_finish<true, true>
+                                       : (const void*)rows::sample_rows_finish<false, true>)
+                           : (long_pen ? (const void*)rows::sample_rows_finish<true, false>
+                                       : (const void*)rows::sample_rows_finish<false, false>);
+    KernelCfg& cfg = shard ? (long_pen ? g_fin_shard_long : g_fin_shard) : (long_pen ? g_fin_long : g_fin);
+    cudaError_t err = configure(cfg, fn, rows::CONSUMERS, fsmem, dev, grid);
+    if (err != cudaSuccess) return err;
+    void* args[] = {const_cast<RowsArgs*>(&a)};
+    err = cudaLaunchKernel(fn, dim3(a.B), dim3(rows::CONSUMERS), args, fsmem, stream);
+    if (err != cudaSuccess) return err;
     return cudaGetLastError();
 }
 }  // namespace

@@ -189,3 +189,27 @@ def test_two_gpu_nccl_matches_unsharded():
     ids, diag, rng_after, hist_after, len_after, hist0, full = res[0]
     seeds, hist_len, hist_head = _state(B)
     _check(ids, diag, rng_after, hist_after, len_after, full, hist0, _params(B), seeds, hist_len, hist_head)
+
+
+@pytest.mark.parametrize("G", [2, 8])
+def test_emulated_shards_min_p_rows_without_top_k(G):
+    """Rows with top_k 0 and a min-p floor: every shard sends all of its keys
+    at or above the floor of the global max, so the merge is exact; one row
+    whose floor lets too many keys through a shard comes back as -1."""
+    import quasar_b200 as q
+    from tests.helpers import gpu_inputs
+    nb = 48
+    logits, hist = gpu_inputs(O.SYNTH_NORMAL, 91, nb, V_FULL, 3.0, H=H, hist_seed=92)
+    prm = O.make_params(nb, temperature=0.9, top_k=0, top_p=0.95, min_p=0.2, repeat_penalty=1.1)
+    prm["min_p"][1::4] = 0.1
+    prm["top_p"][2::4] = 1.0
+    prm["min_p"][nb - 1] = 1e-30   # this row's floor lets thousands of keys through every shard
+    seeds, hist_len, hist_head = _state(nb)
+    # k = 128 keys per shard: room for every min-p survivor of the other rows
+    ids, diag, rng, th, tl = _emulate(logits, hist, prm, seeds, hist_len, hist_head, G, k=128)
+    assert ids[nb - 1] == -1
+    keep = np.arange(nb - 1)
+    ref, ref_rng = O.pick_rows(logits.cpu().numpy()[keep], prm[keep], seeds[keep], hist=hist.cpu().numpy()[keep],
+                               hist_len=hist_len[keep], hist_head=hist_head[keep])
+    assert_parity(ids[keep], diag[keep].view(q.DIAG_DTYPE).reshape(-1), rng[keep].view(np.uint64), ref, ref_rng)
+    assert (ids[keep] >= 0).all()
