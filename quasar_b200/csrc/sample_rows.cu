@@ -114,6 +114,7 @@ struct Buckets {
     uint32_t cnt[NBK];
     uint32_t start[NBK];
 };
+static_assert(sizeof(Buckets) >= CONSUMERS * sizeof(uint64_t), "topk_floor's scratch");
 
 struct Shared {
     int abort;            // a bounded wait gave up
@@ -789,15 +790,39 @@ __device__ __forceinline__ uint32_t deficit_byte(float m, float slotmax) {
 // Lower bound of the k-th largest scaled logit of the row (k <= 256): the
 // k-th largest of the 256 per-thread maxima (256 distinct elements), lowered by
 // a margin that covers ties in p. Rank by (value desc, thread asc).
-__device__ float topk_floor(int k, Shared& s) {
-    const int tid = threadIdx.x;
-    const float mine = s.tfmax[tid];
-    int rank = 0;
-    for (int j = 0; j < CONSUMERS; j++) {
-        const float o = s.tfmax[j];
-        rank += (o > mine || (o == mine && j < tid)) ? 1 : 0;
+// Each warp sorts its 32 maxima (keys ord_key(max) << 32 | (255 - thread):
+// value desc, thread asc) with a shuffle bitonic network and publishes the
+// sorted run in `scratch` (CONSUMERS keys); every thread then ranks the key it
+// holds against the other runs by binary search, and the holder of rank k-1
+// publishes its value.
+__device__ float topk_floor(int k, Shared& s, uint64_t* scratch) {
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    uint64_t key = ((uint64_t)ord_key(s.tfmax[tid]) << 32) | (uint32_t)(CONSUMERS - 1 - tid);
+#pragma unroll
+    for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+        for (int j = size >> 1; j > 0; j >>= 1) {
+            const uint64_t other = __shfl_xor_sync(FULL, key, j);
+            const bool up = (lane & size) != 0;  // size 32: descending over the warp
+            key = (((lane & j) == 0) != up) ? max(key, other) : min(key, other);
+        }
     }
-    if (rank == k - 1) s.pf_lo = mine;
+    scratch[tid] = key;  // lane L holds its warp's L-th largest key
+    csync();
+    int rank = lane;
+#pragma unroll
+    for (int v = 0; v < CWARPS; v++) {
+        if (v == w) continue;
+        const uint64_t* run = scratch + 32 * v;
+        int lo = 0, hi = 32;  // keys of run v greater than this one
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (run[mid] > key) lo = mid + 1;
+            else hi = mid;
+        }
+        rank += lo;
+    }
+    if (rank == k - 1) s.pf_lo = ord_key_inv((uint32_t)(key >> 32));
     csync();
     const float t = s.pf_lo;
     csync();
@@ -1664,10 +1689,11 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
     // (an aborted kernel A leaves stale summaries: keep every index in range)
     const int npen = min(max(__float_as_int(info.z), 0), a.hist_cap);
     R.use_pen = npen > 0;
-    // A list longer than one entry per thread is read twice below: it is
-    // copied once into the bottom of buf (asynchronous copies, all in flight
-    // together), where the candidates appended from the top never reach it.
-    const bool pen_staged = kLongPen && npen > CONSUMERS;
+    // A list longer than one entry per thread (and at most half of buf) is
+    // read twice below: it is copied once into the bottom of buf
+    // (asynchronous copies, all in flight together), where the candidates
+    // appended from the top never reach it.
+    const bool pen_staged = kLongPen && npen > CONSUMERS && npen <= CAP / 2;
     const int2* pen_s = reinterpret_cast<const int2*>(buf);
     if (pen_staged) {
         for (int i = tid; i < npen; i += CONSUMERS) cp_async8(smem_u32(buf + i), pen + i);
@@ -1701,7 +1727,7 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
         if (by_minp) tau = __fadd_rn(R.M, logf(fminf(P.min_p, 1.0f)) - 0.01f);
         if (by_topk) {
             csync();  // every thread's max is in s.tfmax
-            tau = fmaxf(tau, topk_floor(P.top_k, s));
+            tau = fmaxf(tau, topk_floor(P.top_k, s, reinterpret_cast<uint64_t*>(bk)));  // bk is free until the sort
         }
         const float lo = fmaxf(tau, R.thr);
         // qualifying thread-slots -> a shared list (its own area), so the
@@ -2001,6 +2027,132 @@ __global__ void __launch_bounds__(CONSUMERS, 3) sample_rows_finish(RowsArgs a) {
     if ((int)blockIdx.x < a.B) finish_row<kLongPen, kShard>(a, blockIdx.x, buf, bits, bk, qlist, s);  // one row per CTA
 }
 
+// Merge of the vocab shards' candidates, one warp per row (a CTA holds
+// several rows, no block barriers): every shard's k keys arrive sorted (p
+// desc, global id asc, 0-padded), so each key's place in the merged order is
+// its place in its own list plus, per other list, the number of keys greater
+// than it (a binary search). The keys that fall inside the row's kept bound
+// are placed into a warp-private sorted array, and the candidate path's cuts
+// (top-k, top-p, min-p) and draw run over it with warp scans and ballots -
+// the cumulative sums per lane in double, joined by a warp scan, as
+// candidate_cuts does. Greedy rows take the largest key. Shared memory per
+// warp: the G*k gathered keys and the sorted prefix.
+__global__ void __launch_bounds__(256) sample_rows_merge_warp(RowsArgs a) {
+    extern __shared__ __align__(16) unsigned char dyn[];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int G = a.shard_G, k = a.shard_k, n = G * k;
+    uint64_t* keys = reinterpret_cast<uint64_t*>(dyn) + (size_t)w * 2 * n;  // [G][k] gathered
+    uint64_t* sorted = keys + n;                                             // merged prefix
+    const int BEYOND = 0x7FFFFFFF;
+    for (int row = blockIdx.x * nw + w; row < a.B; row += gridDim.x * nw) {
+        const quasar_sample_params pr = a.d_params ? a.d_params[row] : a.h_params;
+        Row R;
+        const RowCtx c = row_ctx(a, row, pr, R);
+        for (int i = lane; i < n; i += 32) {
+            const int g = i / k, j = i - g * k;
+            keys[i] = a.shard_cand[((int64_t)g * a.B + row) * k + j];
+        }
+        __syncwarp();
+        // keys per list (each list is descending, zeros last) and the overflow mark
+        int nk = 0, overflow = 0;
+        uint64_t best = 0ull;
+        for (int i = lane; i < n; i += 32) {
+            const uint64_t key = keys[i];
+            nk += (key >> 32) != 0ull ? 1 : 0;  // real keys carry a nonzero p (or ord_key) part
+            overflow |= key == SHARD_OVERFLOW ? 1 : 0;
+            best = max(best, key);
+        }
+        nk = warp_sum(nk);
+        overflow = __any_sync(FULL, overflow);
+        best = warp_max(best);
+        if (!(pr.temperature > 0.0f)) {
+            // greedy: the largest penalized logit over the shards, lowest
+            // global id on ties (sample.c:130-134)
+            if (lane == 0) write_row(a, row, c, nk > 0 ? (int)(~(uint32_t)best) : 0, 0, 1.0f, 0.0f, QUASAR_PATH_GREEDY, 0ull);
+            __syncwarp();
+            continue;
+        }
+        float M = 0.0f, inv = 0.0f;
+        shard_norm(a, row, M, inv);
+        uint64_t st_rng = a.rng[row];
+        const double u = rng_unit(&st_rng);  // sample.c:173: one step per stochastic row
+        int id = -1, nc = 0;
+        float pch = 0.0f;
+        if (nk > 0 && !overflow) {
+            const RowParams& P = c.P;
+            // the merged prefix that can hold the kept set: top_k keys at most
+            const int L = (P.top_k > 0 && P.top_k < nk) ? P.top_k : nk;
+            for (int i = lane; i < n; i += 32) {
+                const uint64_t key = keys[i];
+                if ((key >> 32) == 0ull) continue;
+                const int g = i / k;
+                int rank = i - g * k;  // keys of its own list above it
+                for (int h = 0; h < G; h++) {
+                    if (h == g) continue;
+                    const uint64_t* lst = keys + h * k;
+                    int lo = 0, hi = k;  // first position whose key is not greater
+                    while (lo < hi) {
+                        const int mid = (lo + hi) >> 1;
+                        if (lst[mid] > key) lo = mid + 1;
+                        else hi = mid;
+                    }
+                    rank += lo;
+                }
+                if (rank < L) sorted[rank] = key;
+            }
+            __syncwarp();
+            auto pval = [&](int i) { return __uint_as_float((uint32_t)(sorted[i] >> 32)); };
+            const int S = (L + 31) / 32;
+            const int i0 = min(lane * S, L), i1 = min(i0 + S, L);
+            double seg = 0.0;
+            for (int i = i0; i < i1; i++) seg += (double)pval(i);
+            const double incl = warp_incl_scan(seg, lane);
+            const double excl = incl - seg;
+            // top-k (sample.c:154), top-p (sample.c:156-160), min-p (sample.c:162-167)
+            const int nc1 = (P.top_k > 0 && P.top_k < nk) ? P.top_k : BEYOND;
+            const int lim = min(nc1, nk);
+            const float floor_p = P.min_p > 0.0f ? __fmul_rn(P.min_p, inv) : 0.0f;
+            int cut_p = BEYOND, cut_m = nk;
+            double cum = excl;
+            for (int i = i0; i < i1; i++) {
+                cum += (double)pval(i);
+                if (P.top_p < 1.0f && i < lim && cut_p == BEYOND && cum >= (double)P.top_p) cut_p = i + 1;
+                if (i >= 1 && cut_m == nk && pval(i) < floor_p) cut_m = i;
+            }
+            cut_p = __reduce_min_sync(FULL, cut_p);
+            cut_m = __reduce_min_sync(FULL, cut_m);
+            const int nc2 = cut_p != BEYOND ? cut_p : nc1;
+            nc = max(1, min(nc2, cut_m));
+            // the kept mass (sample.c:171-172): the cumulative sum at nc - 1
+            double rs = 0.0;
+            if (nc - 1 >= i0 && nc - 1 < i1) {
+                rs = excl;
+                for (int i = i0; i < nc; i++) rs += (double)pval(i);
+            }
+            const int owner = max(__ffs(__ballot_sync(FULL, nc - 1 >= i0 && nc - 1 < i1)) - 1, 0);
+            const double rsum = __shfl_sync(FULL, rs, owner);
+            const double r = u * rsum;  // sample.c:173-175: first kept i with r <= cumsum
+            int cut_d = BEYOND;
+            cum = excl;
+            for (int i = i0; i < min(i1, nc); i++) {
+                cum += (double)pval(i);
+                if (cum >= r) {
+                    cut_d = i;
+                    break;
+                }
+            }
+            cut_d = __reduce_min_sync(FULL, cut_d);
+            const int chosen = cut_d != BEYOND ? cut_d : nc - 1;
+            id = (int)(~(uint32_t)sorted[chosen]);
+            pch = pval(chosen);
+        }
+        // (nk == 0: a shard could not bound its candidates; overflow: a shard
+        // had more min-p survivors than keys to send - the row gets id -1)
+        if (lane == 0) write_row(a, row, c, id, nc, pch, inv, QUASAR_PATH_CANDIDATE, st_rng);
+        __syncwarp();
+    }
+}
+
 // Merge of the vocab shards' candidates, one CTA per row: the G*k gathered
 // keys ([G][B][k]) sorted descending, then greedy rows take the first (the
 // largest penalized logit, lowest global id on ties) and stochastic rows the
@@ -2087,7 +2239,7 @@ struct KernelCfg {
     std::atomic<size_t> smem_set[64];
     std::atomic<int> grid[64];  // resident CTAs of the kernel on each device
 };
-KernelCfg g_ldg, g_tma, g_tma_pick, g_fin, g_fin_long, g_fin_shard, g_fin_shard_long, g_merge;
+KernelCfg g_ldg, g_tma, g_tma_pick, g_fin, g_fin_long, g_fin_shard, g_fin_shard_long, g_merge, g_merge_warp;
 std::mutex g_cfg_mu;
 
 cudaError_t configure(KernelCfg& cfg, const void* fn, int threads, size_t smem, int dev, int& grid) {
@@ -2227,6 +2379,19 @@ cudaError_t launch_shard_merge(const RowsArgs& args, cudaStream_t stream) {
     int dev = 0;
     cudaError_t err = current_device(dev);
     if (err != cudaSuccess) return err;
+    // one warp per row while a warp's keys fit: up to 8 warps per CTA within
+    // 96 KB of shared memory
+    const size_t per_warp = (size_t)16 * args.shard_G * args.shard_k;
+    if (per_warp <= (size_t)96 * 1024) {
+        int warps = (int)min((size_t)8, (size_t)96 * 1024 / per_warp);
+        const size_t wsmem = per_warp * warps;
+        int grid = 0;
+        err = configure(g_merge_warp, (const void*)rows::sample_rows_merge_warp, 32 * warps, wsmem, dev, grid);
+        if (err != cudaSuccess) return err;
+        const int ctas = min((args.B + warps - 1) / warps, grid);
+        rows::sample_rows_merge_warp<<<ctas, 32 * warps, wsmem, stream>>>(args);
+        return cudaGetLastError();
+    }
     const size_t smem = rows_merge_smem_bytes(args.shard_G, args.shard_k);
     int grid = 0;
     err = configure(g_merge, (const void*)rows::sample_rows_merge, rows::CONSUMERS, smem, dev, grid);
