@@ -256,9 +256,24 @@ __device__ __forceinline__ void apply_pen_oct(float* v, uint32_t m, float rp) {
 // finite logits p <= 1; the clamp keeps every key that non-finite logits
 // could produce (inf, NaN, negative NaN bits) at or below the key of 1.0f,
 // so keys always index the histograms and buckets in range.
+// exp(x) rounded once to float (through double). Kept out of line: the
+// whole-row passes of the select path call it from unrolled loops, where an
+// inlined copy per element made the kernel's code too large for the
+// instruction cache.
+#ifndef QS_EXP_NOINLINE
+#define QS_EXP_NOINLINE 1
+#endif
+#if QS_EXP_NOINLINE
+__device__ __noinline__
+#else
+__device__ __forceinline__
+#endif
+float exp_rounded(float x) {
+    return __double2float_rn(exp((double)x));
+}
 __device__ __forceinline__ uint32_t p_key(float sc, float M, float thr, float inv) {
     if (!(sc >= thr)) return 0u;
-    const float e = __double2float_rn(exp((double)__fsub_rn(sc, M)));
+    const float e = exp_rounded(__fsub_rn(sc, M));
     return min(__float_as_uint(__fmul_rn(e, inv)), 0x3F800000u);
 }
 
@@ -295,6 +310,17 @@ __device__ int block_sum_i(int v, Shared& s) {
     return r;
 }
 
+__device__ unsigned long long block_sum_u64(unsigned long long v, Shared& s) {
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) s.rd[threadIdx.x >> 5] = __longlong_as_double((long long)v);
+    csync();
+    unsigned long long r = 0ull;
+#pragma unroll
+    for (int i = 0; i < CWARPS; i++) r += (unsigned long long)__double_as_longlong(s.rd[i]);
+    csync();
+    return r;
+}
+
 // Descending bitonic sort of n (power of two) 64-bit keys in shared memory.
 __device__ void bitonic_desc(uint64_t* a, int n) {
     for (int k = 2; k <= n; k <<= 1) {
@@ -324,8 +350,17 @@ struct Row {
     float rp, inv_t, M, thr, inv;
 };
 
-// Octets in flight per thread in the select path's passes over a row.
-constexpr int SCAN_U = 4;
+// Octets in flight per thread in the select path's passes over a row (2:
+// more unrolling made the passes bound by instruction fetch).
+#ifndef QS_SCAN_U
+#define QS_SCAN_U 2
+#endif
+constexpr int SCAN_U = QS_SCAN_U;
+// The select path's steps, inlined; select_path calls select_row from one
+// loop, so the kernel holds one copy of each pass (its whole-row passes are
+// bound by instruction fetch when the kernel's code outgrows the
+// instruction cache).
+#define QS_SELECT_FN __device__
 
 // Calls f(sc, idx) for every in-range element whose scaled logit lies in
 // [s_lo, s_hi], reading the row from global memory in coalesced octets,
@@ -432,7 +467,7 @@ __device__ void zero_level2(Hist* H) {
 
 // Histogram of key bits [shift, shift+10) over the elements whose key has
 // prefix `prefix` above bit shift+10.
-__device__ void refine(const Row& R, const uint8_t* bits8, Hist* H, uint32_t prefix, int shift,
+QS_SELECT_FN void refine(const Row& R, const uint8_t* bits8, Hist* H, uint32_t prefix, int shift,
                        Shared& s) {
     zero_level2(H);
     const uint32_t klo = prefix << (shift + 10);
@@ -463,7 +498,7 @@ struct Sel {
 
 // Exact select over the row: by_mass -> smallest rank whose cumulative mass
 // reaches target; otherwise the element of rank target-1 (target = rank + 1).
-__device__ Sel select_row(const Row& R, const uint8_t* bits8, Hist* H, bool by_mass,
+QS_SELECT_FN Sel select_row(const Row& R, const uint8_t* bits8, Hist* H, bool by_mass,
                           unsigned long long target, Shared& s) {
     Sel out = {};
     if (by_mass && target == 0ull) target = 1ull;  // every window element carries mass >= 1
@@ -473,6 +508,7 @@ __device__ Sel select_row(const Row& R, const uint8_t* bits8, Hist* H, bool by_m
     unsigned long long m_above = s.bin_mass_above;
     unsigned int c_above = s.bin_cnt_above;
     int n_eq = 0, minid = 0;
+#pragma unroll 1
     for (int level = 0; level < 2; level++) {
         const int shift = level == 0 ? 10 : 0;
         refine(R, bits8, H, prefix, shift, s);
@@ -504,7 +540,7 @@ __device__ Sel select_row(const Row& R, const uint8_t* bits8, Hist* H, bool by_m
 }
 
 // Id of the t-th element (ascending id) whose key equals sel.key.
-__device__ int resolve_id(const Row& R, const uint8_t* bits8, const Sel& sel, Shared& s) {
+QS_SELECT_FN int resolve_id(const Row& R, const uint8_t* bits8, const Sel& sel, Shared& s) {
     if (sel.t == 0) return sel.minid;
     key_range_to_sc(R, sel.key, (uint64_t)sel.key + 1, s);
     const float s_lo = s.pf_lo, s_hi = s.pf_hi;
@@ -558,7 +594,7 @@ __device__ int resolve_id(const Row& R, const uint8_t* bits8, const Sel& sel, Sh
 
 // Select path: exact cuts and draw over the whole row. Publishes res_id,
 // res_nc, res_p.
-__device__ void select_path(const Row& R, const uint8_t* bits8, Hist* H,
+QS_SELECT_FN void select_path(const Row& R, const uint8_t* bits8, Hist* H,
                                          const RowParams& P, double u, Shared& s) {
     for (int i = threadIdx.x; i < NB; i += CONSUMERS) {
         H->cnt1[i] = 0u;
@@ -578,15 +614,8 @@ __device__ void select_path(const Row& R, const uint8_t* bits8, Hist* H,
 
     // top-k (sample.c:154)
     const int nc1 = (P.top_k > 0 && P.top_k < n_window) ? P.top_k : n_window;
-    // top-p (sample.c:156-160)
-    int nc2 = nc1;
-    if (P.top_p < 1.0f) {
-        const unsigned long long tgt = (unsigned long long)ceil((double)P.top_p * 4611686018427387904.0);
-        const Sel sp = select_row(R, bits8, H, true, tgt, s);
-        if (sp.found && sp.rank < nc1) nc2 = sp.rank + 1;
-    }
     // min-p (sample.c:162-167): keep = min(nc, max(1, #{p >= min_p * p_max}))
-    int nc = nc2;
+    int ge = 0x7FFFFFFF;
     if (P.min_p > 0.0f) {
         const float floor_p = __fmul_rn(P.min_p, R.inv);  // p_max = 1 * inv
         const uint32_t fk = __float_as_uint(floor_p);
@@ -603,19 +632,63 @@ __device__ void select_path(const Row& R, const uint8_t* bits8, Hist* H,
                 if (key >= fk && (key >> 20) == fb) in_bin++;
             });
         }
-        const int ge = block_sum_i(above + in_bin, s);
-        nc = min(nc2, max(1, ge));
+        ge = max(1, block_sum_i(above + in_bin, s));
     }
-    if (nc < 1) nc = 1;
-
-    // the last kept element and the kept mass
-    const Sel last = select_row(R, bits8, H, false, (unsigned long long)nc, s);
-    const unsigned long long rsum_fix = last.m_above + (unsigned long long)(last.t + 1) * fixp(last.key);
-    const double rsum = (double)rsum_fix * (1.0 / 4611686018427387904.0);
-    const double r = u * rsum;
-    const unsigned long long tgt = (unsigned long long)ceil(r * 4611686018427387904.0);
-    Sel d = select_row(R, bits8, H, true, tgt, s);
-    if (!d.found || d.rank >= nc) d = last;
+    // Three exact selects, in one loop so that the select code exists once
+    // in the kernel: 0 the top-p position (sample.c:156-160), 1 the last
+    // kept element (its kept mass, sample.c:171-172), 2 the draw position
+    // (sample.c:173-177). Step 1 is skipped when its answer is already
+    // known: the top-p position itself, or every window element (rsum = the
+    // histogram's whole mass).
+    int nc2 = nc1, nc = nc1;
+    Sel last = {}, d = {};
+    double rsum = 0.0;
+#pragma unroll 1
+    for (int step = 0; step < 3; step++) {
+        bool by_mass = true;
+        unsigned long long tgt = 0ull;
+        if (step == 0) {
+            if (!(P.top_p < 1.0f)) continue;
+            tgt = (unsigned long long)ceil((double)P.top_p * 4611686018427387904.0);
+        } else if (step == 1) {
+            nc = max(1, min(nc2, ge));
+            if (nc == n_window && !last.found) {
+                // every window element is kept: the kept mass is the whole histogram's
+                unsigned long long m = 0ull;
+                for (int b = threadIdx.x; b < NB; b += CONSUMERS) m += H->mass1[b];
+                m = block_sum_u64(m, s);
+                rsum = (double)m * (1.0 / 4611686018427387904.0);
+                continue;
+            }
+            if (last.found && last.rank == nc - 1) {  // the top-p position is the last kept element
+                rsum = (double)(last.m_above + (unsigned long long)(last.t + 1) * fixp(last.key)) *
+                       (1.0 / 4611686018427387904.0);
+                continue;
+            }
+            by_mass = false;
+            tgt = (unsigned long long)nc;
+        } else {
+            tgt = (unsigned long long)ceil(u * rsum * 4611686018427387904.0);  // r = u * rsum
+        }
+        const Sel x = select_row(R, bits8, H, by_mass, tgt, s);
+        if (step == 0) {
+            if (x.found && x.rank < nc1) {
+                nc2 = x.rank + 1;
+                last = x;
+            }
+        } else if (step == 1) {
+            last = x;
+            rsum = (double)(last.m_above + (unsigned long long)(last.t + 1) * fixp(last.key)) *
+                   (1.0 / 4611686018427387904.0);
+        } else {
+            d = x;
+        }
+    }
+    if (!d.found || d.rank >= nc) {
+        // the draw fell past the kept set (r at the very end): its last element
+        if (!last.found || last.rank != nc - 1) last = select_row(R, bits8, H, false, (unsigned long long)nc, s);
+        d = last;
+    }
     const int id = resolve_id(R, bits8, d, s);
     if (threadIdx.x == 0) {
         s.res_id = id;
@@ -2038,7 +2111,7 @@ __global__ void __launch_bounds__(CONSUMERS, 3) sample_rows_finish(RowsArgs a) {
 // candidate_cuts does. Greedy rows take the largest key. Shared memory per
 // warp: the G*k gathered keys and the sorted prefix.
 __global__ void __launch_bounds__(256) sample_rows_merge_warp(RowsArgs a) {
-    extern __shared__ __align__(16) unsigned char dyn[];
+    extern __shared__ __align__(128) unsigned char dyn[];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int G = a.shard_G, k = a.shard_k, n = G * k;
     uint64_t* keys = reinterpret_cast<uint64_t*>(dyn) + (size_t)w * 2 * n;  // [G][k] gathered
