@@ -95,6 +95,11 @@ QS_API int qs_ref_sequence(const float *logits, int64_t ld, int n_steps, int V,
                     const qs_params *prm, int repeat_last_n, uint64_t seed,
                     int32_t *ids_out);
 
+/* qs_ref_sequence with each pick's full result (id, kept count, p, margin). */
+QS_API int qs_ref_sequence_diag(const float *logits, int64_t ld, int n_steps, int V,
+                         const qs_params *prm, int repeat_last_n, uint64_t seed,
+                         qs_result *res);
+
 /* The decode loop of a batch: row r gets its own reference object (set up as
  * qs_ref_pick_rows sets it up) and is picked n_steps times on the same logits
  * row, each choice recorded in its ring (sample.c:83-92), as a server that

@@ -70,6 +70,9 @@ def _lib(backend: str) -> ctypes.CDLL:
             lib.qs_ref_sequence.argtypes = [P, ctypes.c_int64, ctypes.c_int, ctypes.c_int, P,
                                             ctypes.c_int, ctypes.c_uint64, P]
             lib.qs_ref_sequence.restype = ctypes.c_int
+            lib.qs_ref_sequence_diag.argtypes = [P, ctypes.c_int64, ctypes.c_int, ctypes.c_int, P,
+                                                 ctypes.c_int, ctypes.c_uint64, P]
+            lib.qs_ref_sequence_diag.restype = ctypes.c_int
             lib.qs_ref_decode.argtypes = [P, ctypes.c_int64, ctypes.c_int, ctypes.c_int, P, ctypes.c_int,
                                           P, ctypes.c_int, P, P, P, ctypes.c_int, P, P, P, P, ctypes.c_int]
             lib.qs_ref_decode.restype = ctypes.c_int
@@ -132,6 +135,18 @@ def ref_sequence(logits: np.ndarray, params: np.ndarray, repeat_last_n: int, see
     if rc != 0:
         raise RuntimeError(f"ref_sequence failed: {rc}")
     return out
+
+
+def ref_sequence_diag(logits: np.ndarray, params: np.ndarray, repeat_last_n: int, seed: int):
+    """ref_sequence with each pick's full result (RESULT_DTYPE: id, kept count, p, margin)."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    n, V = logits.shape
+    res = np.zeros(n, dtype=RESULT_DTYPE)
+    params = np.ascontiguousarray(params, dtype=PARAMS_DTYPE)
+    rc = _lib("ref").qs_ref_sequence_diag(_ptr(logits), V, n, V, _ptr(params), repeat_last_n, seed, _ptr(res))
+    if rc != 0:
+        raise RuntimeError(f"ref_sequence_diag failed: {rc}")
+    return res
 
 
 def ref_decode(logits: np.ndarray, params: np.ndarray, rng: np.ndarray, n_steps: int,

@@ -154,3 +154,18 @@ int qs_ref_decode(const float *logits, int64_t ld, int B, int V,
     if (qs_run_rows(decode_row, &d, B, nthreads) != 0) return -1;
     return d.base.err;
 }
+
+int qs_ref_sequence_diag(const float *logits, int64_t ld, int n_steps, int V,
+                         const qs_params *prm, int repeat_last_n, uint64_t seed,
+                         qs_result *res) {
+    if (seed == 0) return -2;
+    quasar_sampler *s = quasar_sampler_new();
+    if (!s) return -1;
+    quasar_sampler_config(s, prm->temperature, prm->top_p, prm->top_k, prm->min_p,
+                          prm->repeat_penalty, repeat_last_n, seed);
+    int err = 0;
+    for (int t = 0; t < n_steps; t++)
+        if (ref_pick_diag(s, logits + (int64_t)t * ld, V, &res[t]) != 0) err = -3;
+    quasar_sampler_free(s);
+    return err;
+}

@@ -17,6 +17,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libquasar_cuda.so")
+DECODE = os.path.join(HERE, "batched_decode")  # the batched decode driver (batched_decode.c)
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -61,6 +62,16 @@ def build(force: bool = False, verbose: bool = False, ptxas_v: bool = False) -> 
         subprocess.run(cmd, check=True)
     if force or not os.path.exists(LIB) or any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs):
         cmd = [nvcc(), *ARCH, "-shared", "-Xcompiler", "-fPIC", "-o", LIB, *objs, *LINK_LIBS]
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr)
+        subprocess.run(cmd, check=True)
+    # the batched decode driver (host C over the library)
+    drv_src = os.path.join(HERE, "batched_decode.c")
+    if force or not os.path.exists(DECODE) or max(os.path.getmtime(drv_src), os.path.getmtime(LIB)) > \
+            os.path.getmtime(DECODE):
+        cmd = [nvcc(), "-O2", "-Wno-deprecated-gpu-targets", "-I" + INCLUDE, drv_src, "-o", DECODE, "-L" + HERE,
+               "-lquasar_cuda",
+               "-Xlinker", "-rpath=$ORIGIN"]
         if verbose:
             print(" ".join(cmd), file=sys.stderr)
         subprocess.run(cmd, check=True)
