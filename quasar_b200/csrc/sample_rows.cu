@@ -2100,6 +2100,246 @@ __global__ void __launch_bounds__(CONSUMERS, 3) sample_rows_finish(RowsArgs a) {
     if ((int)blockIdx.x < a.B) finish_row<kLongPen, kShard>(a, blockIdx.x, buf, bits, bk, qlist, s);  // one row per CTA
 }
 
+// Descending bitonic sort of n2 (a power of two) keys in shared memory by one warp.
+__device__ void warp_bitonic_desc(uint64_t* a, int n2, int lane) {
+    for (int size = 2; size <= n2; size <<= 1) {
+        for (int j = size >> 1; j > 0; j >>= 1) {
+            for (int i = lane; i < n2; i += 32) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const uint64_t x = a[i], y = a[ixj];
+                    const bool desc = (i & size) == 0;
+                    if (desc ? (x < y) : (x > y)) {
+                        a[i] = y;
+                        a[ixj] = x;
+                    }
+                }
+            }
+            __syncwarp();
+        }
+    }
+}
+
+// Vocab shards, phase 2, one warp per row (shards of up to SW_MAX_COLS
+// columns; a CTA holds SW_WARPS rows, no block barriers). The same cuts as
+// the CTA kernel's candidate mode, found without the tile tables: the row's
+// threshold lo (min-p floor of the global max, the k-th largest per-thread
+// max less its tie margin, the 30-nat window) leaves out every thread of
+// kernel A whose final max is below it, so only the thread-tiles of the
+// other threads (each 16 contiguous columns) are read again; their elements
+// at or above lo, minus the penalized columns, plus the penalized list's
+// entries at or above lo, are the candidates. They are sorted by (p desc,
+// global id asc) and the first k are sent - or, for a min-p row without a
+// top_k <= k, all of them (more than k: the overflow key).
+constexpr int SW_WARPS = 4;
+constexpr int SW_CAP = 512;           // candidates per row
+// shard columns the warp kernel takes: a warp re-reads every tile of the
+// listed threads, so wider shards (the 2-way split of V = 151936: 19 tiles
+// per thread, 342 us per 8192 rows against 208 us for the CTA kernel) keep
+// the CTA kernel; 4- and 8-way splits (10 and 5 tiles) are faster per warp
+constexpr int SW_MAX_COLS = 12 * TILE_ELEMS;
+// Shared memory of one warp: [candidates SW_CAP x 8][listed threads
+// CONSUMERS x 2][penalty bitset over the shard's columns].
+__host__ __device__ inline size_t sw_warp_bytes(int V) {
+    return (size_t)SW_CAP * 8 + CONSUMERS * 2 + (((size_t)(V + 31) / 32 * 4 + 15) & ~(size_t)15);
+}
+struct ShardWarpSmem {
+    uint64_t* cand;
+    uint16_t* thr;
+    uint32_t* bits;
+};
+
+__global__ void __launch_bounds__(32 * SW_WARPS) sample_rows_shard_cand_warp(RowsArgs a) {
+    extern __shared__ __align__(128) unsigned char dyn[];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    unsigned char* base = dyn + (size_t)w * sw_warp_bytes(a.V);
+    ShardWarpSmem sm;
+    sm.cand = reinterpret_cast<uint64_t*>(base);
+    sm.thr = reinterpret_cast<uint16_t*>(base + (size_t)SW_CAP * 8);
+    sm.bits = reinterpret_cast<uint32_t*>(base + (size_t)SW_CAP * 8 + CONSUMERS * 2);
+    const int k = a.shard_k;
+    for (int row = blockIdx.x * SW_WARPS + w; row < a.B; row += gridDim.x * SW_WARPS) {
+        const quasar_sample_params pr = a.d_params ? a.d_params[row] : a.h_params;
+        Row R;
+        const RowCtx c = row_ctx(a, row, pr, R);
+        const RowParams& P = c.P;
+        uint64_t* out = a.shard_cand + (int64_t)row * k;
+        if (!(pr.temperature > 0.0f)) {
+            // greedy: this shard's best column (kernel A), as in the CTA kernel
+            if (lane == 0) {
+                const quasar_shard_stat st = a.all_stats[(int64_t)a.shard_rank * a.B + row];
+                out[0] = st.best >= 0 ? ((uint64_t)ord_key(st.max) << 32) | (uint32_t)(~(uint32_t)(a.col0 + st.best))
+                                      : 0ull;
+            }
+            for (int i = 1 + lane; i < k; i += 32) out[i] = 0ull;
+            __syncwarp();
+            continue;
+        }
+        const bool by_minp = P.min_p > 0.0f;
+        const bool by_topk = P.top_k > 0 && P.top_k <= TOPK_MAX;
+        const bool shard_topk = by_topk && P.top_k <= k;
+        if (!(by_minp || shard_topk)) {
+            // no bound this shard can stand for: no candidates (the merge reports -1)
+            for (int i = lane; i < k; i += 32) out[i] = 0ull;
+            __syncwarp();
+            continue;
+        }
+        const float4 info = a.work_info[row];
+        const int npen = min(max(__float_as_int(info.z), 0), a.hist_cap);
+        shard_norm(a, row, R.M, R.inv);  // the row's global max and 1/sum
+        R.thr = __fsub_rn(R.M, 30.0f);
+        const float* tf = a.work_tfmax + (int64_t)row * CONSUMERS;
+        float lo = -INFINITY;
+        if (by_minp) lo = __fadd_rn(R.M, logf(fminf(P.min_p, 1.0f)) - 0.01f);
+        if (by_topk) {
+            // the k-th largest per-thread max (topk_floor's value), by a radix
+            // select over the order-preserving keys, 8 per lane, bit by bit
+            uint32_t key8[CONSUMERS / 32];
+#pragma unroll
+            for (int q = 0; q < CONSUMERS / 32; q++) key8[q] = ord_key(tf[q * 32 + lane]);
+            uint32_t prefix = 0u;
+            int need = P.top_k;  // rank (1-based) of the wanted key among those matching prefix
+#pragma unroll 1
+            for (int b = 31; b >= 0; b--) {
+                const uint32_t want = (prefix << 1) | 1u;  // the bit-b-set half sorts first
+                int c = 0;
+#pragma unroll
+                for (int q = 0; q < CONSUMERS / 32; q++) c += ((key8[q] >> b) == want) ? 1 : 0;
+                c = __reduce_add_sync(FULL, c);
+                if (c >= need) {
+                    prefix = want;
+                } else {
+                    prefix = want - 1u;
+                    need -= c;
+                }
+            }
+            const float t = ord_key_inv(prefix);
+            lo = fmaxf(lo, !(t > -INFINITY) ? -INFINITY : t - (1e-5f + 1e-5f * fabsf(t)));
+        }
+        lo = fmaxf(lo, R.thr);
+        // the penalized columns of this shard (their re-read values are raw)
+        const int nwords = (R.V + 31) >> 5;
+        for (int i = lane; i < nwords; i += 32) sm.bits[i] = 0u;
+        __syncwarp();
+        const int2* pen = a.work_pen + (int64_t)row * a.hist_cap;
+        for (int i = lane; i < npen; i += 32) {
+            const int id = pen[i].x;
+            if (id >= 0 && id < R.V) atomicOr(&sm.bits[id >> 5], 1u << (id & 31));
+        }
+        // kernel A threads whose final max reaches lo
+        int nthr = 0;
+        for (int base = 0; base < CONSUMERS; base += 32) {
+            const bool q = tf[base + lane] >= lo;
+            const unsigned bal = __ballot_sync(FULL, q);
+            if (q) sm.thr[nthr + __popc(bal & ((1u << lane) - 1u))] = (uint16_t)(base + lane);
+            nthr += __popc(bal);
+        }
+        __syncwarp();
+        // their thread-tiles (16 contiguous columns each), two per lane per
+        // round with all four loads in flight
+        const int nitems = nthr * R.ntiles;
+        int ncand = 0;
+        for (int base = 0; base < nitems; base += 64) {
+            uint32_t mk[2] = {0u, 0u};
+            float v[2][16];
+            int e0[2] = {0, 0};
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int i = base + h * 32 + lane;
+                if (i < nitems) {
+                    const int t = sm.thr[i / R.ntiles], it = i - (i / R.ntiles) * R.ntiles;
+                    const int o0 = it * OCT_TILE + 2 * t;
+                    e0[h] = 8 * o0;
+                    load_oct_keep(R.ptr, o0, R.V, R.vec, v[h]);
+                    load_oct_keep(R.ptr, o0 + 1, R.V, R.vec, v[h] + 8);
+                    mk[h] = 0xFFFFu;
+                }
+            }
+            int cnt = 0;
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                if (mk[h]) {
+                    uint32_t m = 0u;
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        const int idx = e0[h] + j;
+                        v[h][j] = __fmul_rn(v[h][j], R.inv_t);  // sample.c:142
+                        const bool pen_col = idx < R.V && ((sm.bits[idx >> 5] >> (idx & 31)) & 1u);
+                        m |= (idx < R.V && !pen_col && v[h][j] >= lo ? 1u : 0u) << j;
+                    }
+                    mk[h] = m;
+                }
+                cnt += __popc(mk[h]);
+            }
+            const int incl = warp_incl_scan(cnt, lane);
+            int pos = ncand + incl - cnt;
+            ncand += __shfl_sync(FULL, incl, 31);
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    if (mk[h] & (1u << j)) {
+                        if (pos < SW_CAP)
+                            sm.cand[pos] = ((uint64_t)__float_as_uint(v[h][j]) << 32) | (uint32_t)(e0[h] + j);
+                        pos++;
+                    }
+                }
+            }
+        }
+        // the penalized columns at or above lo, with their penalized values
+        for (int base = 0; base < npen; base += 32) {
+            const int i = base + lane;
+            bool keep = false;
+            int2 pe = make_int2(0, 0);
+            if (i < npen) {
+                pe = pen[i];
+                keep = pe.x >= 0 && pe.x < R.V && __int_as_float(pe.y) >= lo;
+            }
+            const unsigned bal = __ballot_sync(FULL, keep);
+            const int pos = ncand + __popc(bal & ((1u << lane) - 1u));
+            if (keep && pos < SW_CAP) sm.cand[pos] = ((uint64_t)(uint32_t)pe.y << 32) | (uint32_t)pe.x;
+            ncand += __popc(bal);
+        }
+        __syncwarp();
+        if (ncand > SW_CAP || (!shard_topk && ncand > k)) {
+            // more candidates than this shard can hold or send
+            for (int i = lane; i < k; i += 32) out[i] = i == 0 ? SHARD_OVERFLOW : 0ull;
+            __syncwarp();
+            continue;
+        }
+        // keys (p desc, global id asc); each key's rank is the number of
+        // larger keys (all distinct: the id is part of the key), and the
+        // first k by rank go out in order
+        for (int i = lane; i < ncand; i += 32) {
+            const uint64_t en = sm.cand[i];
+            const uint32_t pk = p_key(__uint_as_float((uint32_t)(en >> 32)), R.M, R.thr, R.inv);
+            sm.cand[i] = ((uint64_t)pk << 32) | (uint32_t)(~(uint32_t)(a.col0 + (int64_t)(uint32_t)en));
+        }
+        __syncwarp();
+        constexpr int PER = 4;  // keys a lane ranks per sweep
+        for (int b0 = 0; b0 < ncand; b0 += 32 * PER) {
+            uint64_t mine[PER];
+            int rank[PER];
+#pragma unroll
+            for (int q = 0; q < PER; q++) {
+                const int i = b0 + q * 32 + lane;
+                mine[q] = i < ncand ? sm.cand[i] : 0ull;
+                rank[q] = 0;
+            }
+            for (int j = 0; j < ncand; j++) {
+                const uint64_t o = sm.cand[j];  // the same j for every lane: one broadcast read
+#pragma unroll
+                for (int q = 0; q < PER; q++) rank[q] += o > mine[q] ? 1 : 0;
+            }
+#pragma unroll
+            for (int q = 0; q < PER; q++)
+                if (b0 + q * 32 + lane < ncand && rank[q] < k) out[rank[q]] = mine[q];
+        }
+        for (int i = ncand + lane; i < k; i += 32) out[i] = 0ull;
+        __syncwarp();
+    }
+}
+
 // Merge of the vocab shards' candidates, one warp per row (a CTA holds
 // several rows, no block barriers): every shard's k keys arrive sorted (p
 // desc, global id asc, 0-padded), so each key's place in the merged order is
@@ -2312,7 +2552,8 @@ struct KernelCfg {
     std::atomic<size_t> smem_set[64];
     std::atomic<int> grid[64];  // resident CTAs of the kernel on each device
 };
-KernelCfg g_ldg, g_tma, g_tma_pick, g_fin, g_fin_long, g_fin_shard, g_fin_shard_long, g_merge, g_merge_warp;
+KernelCfg g_ldg, g_tma, g_tma_pick, g_fin, g_fin_long, g_fin_shard, g_fin_shard_long, g_merge, g_merge_warp,
+    g_shard_warp;
 std::mutex g_cfg_mu;
 
 cudaError_t configure(KernelCfg& cfg, const void* fn, int threads, size_t smem, int dev, int& grid) {
@@ -2439,6 +2680,16 @@ cudaError_t launch_shard_candidates(const RowsArgs& args, void* workspace, cudaS
     int dev = 0;
     cudaError_t err = current_device(dev);
     if (err != cudaSuccess) return err;
+    if (a.V <= rows::SW_MAX_COLS) {  // one warp per row
+        const size_t smem = rows::SW_WARPS * rows::sw_warp_bytes(a.V);
+        int grid = 0;
+        err = configure(g_shard_warp, (const void*)rows::sample_rows_shard_cand_warp, 32 * rows::SW_WARPS, smem, dev,
+                        grid);
+        if (err != cudaSuccess) return err;
+        const int ctas = min((a.B + rows::SW_WARPS - 1) / rows::SW_WARPS, grid);
+        rows::sample_rows_shard_cand_warp<<<ctas, 32 * rows::SW_WARPS, smem, stream>>>(a);
+        return cudaGetLastError();
+    }
     return launch_finish(a, dev, stream);
 }
 
