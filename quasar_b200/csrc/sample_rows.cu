@@ -903,6 +903,65 @@ __device__ float topk_floor(int k, Shared& s, uint64_t* scratch) {
     return t - (1e-5f + 1e-5f * fabsf(t));
 }
 
+// Lower bound of the kept prefix of a row cut by top-p alone (sample.c:
+// 155-160), from the 256 per-thread maxima: sorted descending (warp sorts,
+// then ranks, as topk_floor), with their exact p (p_key) summed in double
+// down the order, the first maximum where the sum reaches top_p (with a
+// 1e-9 safety margin) bounds the prefix - every element at or above it
+// carries at least that mass, so the top-p cut falls among them. Returns
+// that value less topk_floor's tie margin, or -inf when the maxima do not
+// carry top_p. Uses `scratch` (2 KB) and s.tfmax; all consumer threads.
+__device__ float topp_floor(float top_p, const Row& R, Shared& s, uint64_t* scratch) {
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    uint64_t key = ((uint64_t)ord_key(s.tfmax[tid]) << 32) | (uint32_t)(CONSUMERS - 1 - tid);
+#pragma unroll
+    for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+        for (int j = size >> 1; j > 0; j >>= 1) {
+            const uint64_t other = __shfl_xor_sync(FULL, key, j);
+            const bool up = (lane & size) != 0;
+            key = (((lane & j) == 0) != up) ? max(key, other) : min(key, other);
+        }
+    }
+    scratch[tid] = key;
+    csync();
+    int rank = lane;
+#pragma unroll
+    for (int v = 0; v < CWARPS; v++) {
+        if (v == w) continue;
+        const uint64_t* run = scratch + 32 * v;
+        int lo = 0, hi = 32;
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (run[mid] > key) lo = mid + 1;
+            else hi = mid;
+        }
+        rank += lo;
+    }
+    csync();  // every run is read
+    // the values in rank order (the thread holding rank r writes slot r)
+    float* sorted = reinterpret_cast<float*>(scratch);
+    const float val = ord_key_inv((uint32_t)(key >> 32));
+    sorted[rank] = val;
+    if (tid == 0) s.cut_p = 0x7FFFFFFF;
+    csync();
+    // this thread takes rank tid: its p and the double sum down to it
+    const float mv = sorted[tid];
+    const double pv = (double)__uint_as_float(p_key(mv, R.M, R.thr, R.inv));
+    const double incl = warp_incl_scan(pv, lane);
+    if (lane == 31) s.rd[w] = incl;
+    csync();
+    double cum = incl;
+    for (int v = 0; v < w; v++) cum += s.rd[v];
+    if (cum >= (double)top_p + 1e-9) atomicMin(&s.cut_p, tid);
+    csync();
+    const int j = s.cut_p;
+    const float t = j < CONSUMERS ? sorted[j] : -INFINITY;
+    csync();  // sorted and cut_p are read before any later use
+    if (!(t > -INFINITY)) return -INFINITY;
+    return t - (1e-5f + 1e-5f * fabsf(t));
+}
+
 // Minimum and maximum of an unsigned value over the consumer threads.
 __device__ void block_minmax_u(uint32_t& lo, uint32_t& hi, Shared& s) {
     lo = __reduce_min_sync(FULL, lo);
@@ -1794,8 +1853,20 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
     // above the min-p threshold of the global max (at most k of them: more
     // are reported as an overflow, see below).
     const bool shard_topk = by_topk && P.top_k <= a.shard_k;
-    if (!(a.flags & QUASAR_FLAG_EXACT_SELECT) && (by_minp || by_topk) && (!shard || shard_topk || by_minp)) {
-        float tau = -INFINITY;
+    // A row cut by top-p alone: when the per-thread maxima (each a real
+    // element) above some value already carry the top-p mass, the kept
+    // prefix lies above that value and the candidate path takes the row
+    // (topp_floor); otherwise the select path.
+    float tau_p = -INFINITY;
+    bool by_topp = false;
+    if (!kShard && !by_minp && !by_topk && P.top_p < 1.0f && !(a.flags & QUASAR_FLAG_EXACT_SELECT)) {
+        csync();  // every thread's max is in s.tfmax
+        tau_p = topp_floor(P.top_p, R, s, reinterpret_cast<uint64_t*>(bk));
+        by_topp = tau_p > -INFINITY;
+    }
+    if (!(a.flags & QUASAR_FLAG_EXACT_SELECT) && (by_minp || by_topk || by_topp) &&
+        (!shard || shard_topk || by_minp)) {
+        float tau = tau_p;
         // (logf is within a few ulp: far inside the 0.01 margin)
         if (by_minp) tau = __fadd_rn(R.M, logf(fminf(P.min_p, 1.0f)) - 0.01f);
         if (by_topk) {

@@ -298,3 +298,27 @@ def test_strided_and_unaligned_rows(offset, extra):
     ids, diag, rng = run_gpu(logits, prm, seeds)
     res, rng_ref = run_oracle(src, prm, seeds)
     assert_parity(ids, diag, rng, res, rng_ref)
+
+
+def test_top_p_only_rows_bounded_by_thread_maxima():
+    """Rows cut by top-p alone: where the per-thread maxima above some value
+    already carry the top-p mass (peaked rows: low temperature), the row
+    takes the candidate path with that value as its threshold; flat rows
+    (high temperature) keep the select path. Both match the reference, and
+    the bounded rows match the exact select path bit for bit."""
+    B = 64
+    logits, hist = gpu_inputs(O.SYNTH_NORMAL, 61, B, V_FULL, 3.0, H=64, hist_seed=62)
+    temps = np.linspace(0.15, 1.5, B).astype(np.float32)
+    prm = O.make_params(B, temperature=temps, top_p=0.9, repeat_penalty=1.1)
+    seeds = _seeds(B, 4242)
+    ids, diag, rng = run_gpu(logits, prm, seeds, hist=hist)
+    res, rng_ref = run_oracle(logits, prm, seeds, hist=hist)
+    assert_parity(ids, diag, rng, res, rng_ref)
+    paths = diag["path"]
+    assert (paths[:8] == 1).all(), paths      # the coolest rows are bounded
+    assert (paths[-8:] == 2).all(), paths     # the flattest are not
+    ids_s, diag_s, rng_s = run_gpu(logits, prm, seeds, hist=hist, flags=1)
+    bounded = paths == 1
+    assert np.array_equal(ids[bounded], ids_s[bounded])
+    assert np.array_equal(diag["n_kept"][bounded], diag_s["n_kept"][bounded])
+    assert np.array_equal(diag["p_chosen"][bounded].view(np.uint32), diag_s["p_chosen"][bounded].view(np.uint32))

@@ -46,6 +46,7 @@ def test_noalloc_matches_pick_batch_two_calls():
     prm = q.make_params(B, temperature=temps, top_p=0.95, min_p=0.05, repeat_penalty=1.1)
     prm["temperature"][::7] = 0.0          # some greedy rows
     prm["min_p"][3::11] = 0.0              # some rows on the exact-select path
+    prm["top_p"][3::11] = 1.0              # (pure multinomial: no bound keeps them off it)
     d_params = q.params_to_device(prm, logits.device)
     seeds = np.arange(1, B + 1, dtype=np.uint64) * np.uint64(0x9E3779B97F4A7C15)
     stream = torch.cuda.current_stream()
