@@ -1414,6 +1414,13 @@ __device__ __forceinline__ void pick_penalized(const Row& R, uint8_t* bits8, con
             unpack2(lo, v[4 * k], v[4 * k + 1]);
             unpack2(hi, v[4 * k + 2], v[4 * k + 3]);
         }
+        // list positions: one shared atomic per warp for all of its picks
+        // (the whole warp is here: the branch condition is warp-uniform)
+        const int cnt = __popc(mb);
+        const int incl = warp_incl_scan(cnt, (int)threadIdx.x & 31);
+        int pos = 0;
+        if ((threadIdx.x & 31) == 31) pos = atomicAdd(npen, incl);
+        pos = __shfl_sync(FULL, pos, 31) + incl - cnt;
         if (mb) {
             *reinterpret_cast<uint16_t*>(bits8 + o0) = 0;
             uint32_t b = mb;
@@ -1423,7 +1430,7 @@ __device__ __forceinline__ void pick_penalized(const Row& R, uint8_t* bits8, con
                 float x;
                 asm volatile("ld.shared.f32 %0, [%1];" : "=f"(x) : "r"((stage ^ (16u * (uint32_t)(j >> 2))) + 4u * (uint32_t)(j & 3)));
                 const float sc = __fmul_rn(penalize(x, R.rp), R.inv_t);
-                pen[atomicAdd(npen, 1)] = make_int2(reg_elem(it, (int)threadIdx.x, j), __float_as_int(sc));
+                pen[pos++] = make_int2(reg_elem(it, (int)threadIdx.x, j), __float_as_int(sc));
                 m = fmaxf(m, sc);
                 if (sc > m_ref + REF_SLACK) {
                     S = S * exp((double)m_ref - (double)sc) + 1.0;

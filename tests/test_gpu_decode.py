@@ -113,3 +113,17 @@ def test_mixed_params_decode_loop_from_empty_rings():
     seeds = np.arange(1, B + 1, dtype=np.uint64) * np.uint64(0x9E3779B97F4A7C15)
     gpu, ref = _decode(B, H, steps, prm, seeds, O.SYNTH_NORMAL, 2.0, 41, 42, np.zeros(B, np.int32))
     print(_compare(gpu, ref, prm))
+
+
+def test_long_history_decode_loop_picks_penalties_in_stream():
+    """Rings of 512 slots (more than the streaming kernel's 256 threads: the
+    instance that picks penalized values up from its ring while streaming)
+    filling from empty, with greedy rows (which still claim) mixed in, 64
+    steps under a strong repeat penalty."""
+    B, H, steps = 24, 512, 64
+    prm = O.make_params(B, temperature=1.0, top_p=1.0, min_p=0.1, repeat_penalty=1.5)
+    prm["temperature"][::4] = 0.0
+    prm["top_k"][1::4] = 20
+    seeds = np.arange(3, B + 3, dtype=np.uint64) * np.uint64(0x9E3779B97F4A7C15)
+    gpu, ref = _decode(B, H, steps, prm, seeds, O.SYNTH_ZIPF, 1.1, 71, 72, np.zeros(B, np.int32))
+    print(_compare(gpu, ref, prm))
