@@ -384,8 +384,9 @@ def run_latency(args) -> None:
     (quasar_sampler_pick) on a host row and on a device row (wall clock per
     call: each call blocks until the id is on the host), and
     quasar_sampler_pick_batch with B=1 on device-resident state (CUDA events
-    over back-to-back calls). The reference sample.c, one core, on the same
-    row is the CPU figure."""
+    over back-to-back calls), the last also at B = 4 and 16 and with each
+    row on one CTA (QUASAR_FLAG_NO_SPLIT) beside the default column split.
+    The reference sample.c, one core, on the same row is the CPU figure."""
     import torch
     import quasar_b200 as q
     from oracle import oracle as O
@@ -413,29 +414,41 @@ def run_latency(args) -> None:
 
     host_ms, host_p90 = drop_in(host)
     dev_ms, dev_p90 = drop_in(row[0])
-    # pick_batch, B = 1, state on the device, calls back to back
-    hist = torch.empty(1, 64, dtype=torch.int32, device=dev)
-    q.synth_hist(42, 0, 1, 64, V, hist)
-    hl = torch.full((1,), 64, dtype=torch.int32, device=dev)
-    hh = torch.zeros(1, dtype=torch.int32, device=dev)
-    rng = torch.tensor([42], dtype=torch.int64, device=dev)
-    out = torch.empty(1, dtype=torch.int32, device=dev)
-    ws = torch.empty(q.workspace_bytes(1, 64) + 256, dtype=torch.uint8, device=dev)
-    wsv = ws[(-ws.data_ptr()) % 256:][:q.workspace_bytes(1, 64)]
     prm = q.make_params(1, **kw)
     stream = torch.cuda.current_stream(dev)
-    for _ in range(max(args.warmup, 3)):
-        q.pick_batch(row, rng, params=prm, hist=hist, hist_len=hl, hist_head=hh, record=True, out=out,
-                     workspace=wsv, stream=stream)
-    torch.cuda.synchronize(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(steps):
-        q.pick_batch(row, rng, params=prm, hist=hist, hist_len=hl, hist_head=hh, record=True, out=out,
-                     workspace=wsv, stream=stream)
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    batch_ms = e0.elapsed_time(e1) / steps
+
+    def batch_ms(B, flags):
+        """pick_batch over B rows (config 1's parameters), state on the
+        device, calls back to back: CUDA events per call."""
+        rows = torch.empty(B, V, dtype=torch.float32, device=dev)
+        q.synth_logits(q.SYNTH_NORMAL, 42, 0, B, V, 3.0, rows)
+        hist = torch.empty(B, 64, dtype=torch.int32, device=dev)
+        q.synth_hist(42, 0, B, 64, V, hist)
+        hl = torch.full((B,), 64, dtype=torch.int32, device=dev)
+        hh = torch.zeros(B, dtype=torch.int32, device=dev)
+        rng = torch.arange(42, 42 + B, dtype=torch.int64, device=dev)
+        out = torch.empty(B, dtype=torch.int32, device=dev)
+        nb = q.workspace_bytes(B, 64)
+        ws = torch.empty(nb + 256, dtype=torch.uint8, device=dev)
+        wsv = ws[(-ws.data_ptr()) % 256:][:nb]
+        for _ in range(max(args.warmup, 3)):
+            q.pick_batch(rows, rng, params=prm, hist=hist, hist_len=hl, hist_head=hh, record=True, out=out,
+                         workspace=wsv, flags=flags, stream=stream)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            q.pick_batch(rows, rng, params=prm, hist=hist, hist_len=hl, hist_head=hh, record=True, out=out,
+                         workspace=wsv, flags=flags, stream=stream)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / steps
+
+    small = {}
+    for B in (1, 4, 16):
+        small[f"pick_batch_B{B}_split{q.split_shards(B, V, params=prm, hist_cap=64)}_per_call"] = batch_ms(B, 0)
+        small[f"pick_batch_B{B}_one_cta_per_row_per_call"] = batch_ms(B, q.FLAG_NO_SPLIT)
+    batch_ms1 = small["pick_batch_B1_split%d_per_call" % q.split_shards(1, V, params=prm, hist_cap=64)]
     # the reference sample.c on one core, the same row and parameters
     n_ref = 10
     t0 = time.perf_counter()
@@ -449,9 +462,10 @@ def run_latency(args) -> None:
                                    "repeat_penalty 1.1 over the last 64 ids, seed 42"},
             "latency_ms": {"drop_in_host_row_p50": host_ms, "drop_in_host_row_p90": host_p90,
                            "drop_in_device_row_p50": dev_ms, "drop_in_device_row_p90": dev_p90,
-                           "pick_batch_B1_device_per_call": batch_ms},
+                           "pick_batch_B1_device_per_call": batch_ms1, **small},
+            "split_shards_B1": q.split_shards(1, V, params=prm, hist_cap=64),
             "e2e": {"value": host_ms, "unit": "ms", "h2d_bytes_per_step": V * 4, "d2h_bytes_per_step": 4},
-            "gpu_launches": steps * 2,
+            "gpu_launches": steps * (3 if q.split_shards(1, V, params=prm, hist_cap=64) else 2),
             "cpu_baseline": {"value": ref_ms, "unit": "ms", "cores": 1, "kind": "reference",
                              "sample": f"{n_ref} picks of the same row through one reference sampler object"}}
     print(json.dumps(line), flush=True)

@@ -17,7 +17,7 @@ STATUS = {0: "ok", -1: "invalid argument", -2: "unsupported shape", -3: "CUDA er
           -4: "out of memory", -5: "NCCL error", -6: "buffer overflow"}
 
 PATH_GREEDY, PATH_CANDIDATE, PATH_SELECT = 0, 1, 2
-FLAG_EXACT_SELECT = 1
+FLAG_EXACT_SELECT, FLAG_NO_TMA, FLAG_NO_SPLIT = 1, 2, 4
 QUASAR_NOALLOC_WORKSPACE_BYTES = 32 << 20  # include/quasar_sampler.h
 SYNTH_NORMAL, SYNTH_GUMBEL_PEAK, SYNTH_ZIPF = 0, 1, 2
 
@@ -38,6 +38,7 @@ SIGNATURES = {
     "quasar_sampler_pick_batch": ([_P, _I64, _I, _I, _P, _P, _P, _P, _I, _P, _P, _I, _P, _P,
                                    _P, ctypes.c_size_t, _I, _P], _I),
     "quasar_sampler_pick_batch_launches": ([], _I),
+    "quasar_sampler_split_shards": ([_P, _I64, _I, _I, _P, _P, _I, _I], _I),
     "quasar_sampler_pick_batch_noalloc": ([_P, _I64, _I, _I, _P, _P, _P, _P, _I, _P, _P, _I, _P, _P,
                                            _I, _P], _I),
     "quasar_sampler_workspace_bytes": ([_I, _I], ctypes.c_size_t),

@@ -138,8 +138,9 @@ int sync_config(quasar_sampler* s) {
             return QUASAR_ECUDA;
         s->hist_cap = s->repeat_last_n;
     }
-    // this object's own workspace for a one-row pick with its ring
-    rc = object_workspace(s, qs::rows_workspace_bytes(1, s->hist_cap));
+    // this object's own workspace for a one-row pick with its ring (split
+    // into column shards when its parameters allow)
+    rc = object_workspace(s, quasar_sampler_workspace_bytes(1, s->hist_cap));
     if (rc != QUASAR_OK) return rc;
     if (s->rng_dirty) {
         if (cudaMemcpyAsync(s->d_rng, &s->seed_state, sizeof(uint64_t), cudaMemcpyHostToDevice,
@@ -193,8 +194,30 @@ const char* quasar_status_string(int status) {
 
 int quasar_sampler_pick_batch_launches(void) { return 2; }
 
+int quasar_sampler_split_shards(const float* d_logits, int64_t ld, int B, int V,
+                                const quasar_sample_params* d_params, const quasar_sample_params* h_params,
+                                int hist_cap, int flags) {
+    if (B < 1 || V < 1 || V > QUASAR_MAX_VOCAB || ld < V || (!d_params && !h_params) || hist_cap < 0) return 0;
+    qs::RowsArgs a;
+    memset(&a, 0, sizeof a);
+    a.B = B;
+    a.V = V;
+    a.d_params = d_params;
+    if (h_params) a.h_params = *h_params;
+    a.hist = hist_cap > 0 ? reinterpret_cast<int32_t*>(1) : nullptr;  // only its presence is read
+    a.hist_cap = hist_cap;
+    a.flags = flags;
+    a.tma = qs::rows_tma_ok(d_logits, ld, V) && !(flags & QUASAR_FLAG_NO_TMA);
+    const int G = qs::split_shards(a);
+    return G > 0 && qs::split_workspace_bytes(B, G, hist_cap) <= quasar_sampler_workspace_bytes(B, hist_cap) ? G : 0;
+}
+
 size_t quasar_sampler_workspace_bytes(int B, int hist_cap) {
-    return B > 0 ? qs::rows_workspace_bytes(B, hist_cap) : 0;
+    if (B <= 0) return 0;
+    const size_t rows = qs::rows_workspace_bytes(B, hist_cap);
+    if (B > qs::SPLIT_MAX_B) return rows;
+    const size_t split = qs::split_workspace_bytes(B, 0, hist_cap);
+    return split > rows ? split : rows;
 }
 
 int quasar_sampler_pick_batch(const float* d_logits, int64_t ld, int B, int V,
@@ -227,16 +250,24 @@ int quasar_sampler_pick_batch(const float* d_logits, int64_t ld, int B, int V,
     a.vec = ((uintptr_t)d_logits % 32 == 0) && (ld % 8 == 0);
     a.tma = qs::rows_tma_ok(d_logits, ld, V) && !(flags & QUASAR_FLAG_NO_TMA);
     const cudaStream_t st = (cudaStream_t)stream;
+    // a small batch with host parameters: G column shards per row (0: one CTA per row)
+    const int G = qs::split_shards(a);
+    const size_t split_bytes = G > 0 ? qs::split_workspace_bytes(B, G, hist_cap) : 0;
     if (d_workspace) {
         if (workspace_bytes < qs::rows_workspace_bytes(B, hist_cap) || (uintptr_t)d_workspace % 256 != 0)
             return QUASAR_EINVAL;
-        return qs::launch_sample_rows(a, d_workspace, st) == cudaSuccess ? QUASAR_OK : QUASAR_ECUDA;
+        const cudaError_t err = G > 0 && workspace_bytes >= split_bytes
+                                    ? qs::launch_split_rows(a, G, d_workspace, st)
+                                    : qs::launch_sample_rows(a, d_workspace, st);
+        return err == cudaSuccess ? QUASAR_OK : QUASAR_ECUDA;
     }
     std::lock_guard<std::mutex> lock(g_ws_mu);  // held until the launch is queued
     void* ws = nullptr;
-    const int wrc = managed_workspace(qs::rows_workspace_bytes(B, hist_cap), st, &ws);
+    const size_t rows_bytes = qs::rows_workspace_bytes(B, hist_cap);
+    const int wrc = managed_workspace(split_bytes > rows_bytes ? split_bytes : rows_bytes, st, &ws);
     if (wrc != QUASAR_OK) return wrc;
-    return qs::launch_sample_rows(a, ws, st) == cudaSuccess ? QUASAR_OK : QUASAR_ECUDA;
+    const cudaError_t err = G > 0 ? qs::launch_split_rows(a, G, ws, st) : qs::launch_sample_rows(a, ws, st);
+    return err == cudaSuccess ? QUASAR_OK : QUASAR_ECUDA;
 }
 
 quasar_sampler* quasar_sampler_new(void) {

@@ -1073,6 +1073,7 @@ __device__ __forceinline__ int reg_elem(int it, int tid, int j) {
 struct LdgSource {
     static constexpr bool kRegs = true;
     static constexpr bool kPick = false;  // penalized values are claimed at the row's end
+    static constexpr bool kSplit = false;
     float nxt[LDG_DEPTH][16];  // tiles it+1 .. it+LDG_DEPTH in flight
     __device__ __forceinline__ void begin(const Row& R) {
 #pragma unroll
@@ -1118,11 +1119,13 @@ __device__ __noinline__ bool ring_wait_slow(uint32_t bar, uint32_t par, int* abo
 
 // kPickable: stochastic rows with long histories pick their penalized values
 // up from the ring (a separate kernel instance, so the common case's code is
-// not affected by it).
-template <bool kPickable>
+// not affected by it). kSplit: a split launch (launch rows are column shards,
+// state_row), also an instance of its own.
+template <bool kPickable, bool kSplitRows>
 struct TmaSource {
     static constexpr bool kRegs = false;
     static constexpr bool kPick = kPickable;
+    static constexpr bool kSplit = kSplitRows;
     uint32_t ring_u32;  // NSTAGE tiles (shared-window address)
     uint32_t thr_off;   // 64 * tid + 16 * chunk_swz(tid)
     uint32_t full0, empty0;
@@ -1217,6 +1220,20 @@ __device__ __forceinline__ RowCtx row_ctx(const RowsArgs& a, int row, const quas
     return row_ctx_raw(a, row, pr, ring_len_raw(a, row), ring_head_raw(a, row), R);
 }
 
+// Split launches (a.split_B > 0): launch row `row` is column shard
+// row / split_B of state row row % split_B. state_row gives the index of the
+// row's parameters, PRNG word and ring; split_shard points c and R (set up
+// for the state row) at the shard's columns.
+template <bool kSplit>
+__device__ __forceinline__ int state_row(const RowsArgs& a, int row) {
+    if constexpr (kSplit) return row % a.split_B;
+    else return row;
+}
+__device__ __forceinline__ void split_shard(const RowsArgs& a, int row, int srow, RowCtx& c, Row& R) {
+    c.col0 = (int64_t)(row / a.split_B) * a.V;
+    R.ptr = a.logits + (int64_t)srow * a.ld + c.col0;
+}
+
 // row_ctx plus the penalty bitset of the row's history ids (consumer threads).
 // my_id: this thread's ring entry (threadIdx.x) when it is a column id, else
 // -1; its logit is copied into s.tfmax[threadIdx.x] (idle in kernel A) while
@@ -1229,9 +1246,11 @@ __device__ __forceinline__ bool ring_slot_used(const RowCtx& c, int p) {
 // Copies the inputs row_setup needs for `row` into shared memory (cp.async,
 // one group): parameters, ring length and head, ring slots 0..CONSUMERS-1
 // (raw positions, into tfmax). Rows past B are skipped.
-__device__ __forceinline__ void stage_next_row(const RowsArgs& a, int row, SharedA& s) {
+template <bool kSplit>
+__device__ __forceinline__ void stage_next_row(const RowsArgs& a, int lrow, SharedA& s) {
     const int tid = threadIdx.x;
-    if (row < a.B) {
+    if (lrow < a.B) {
+        const int row = state_row<kSplit>(a, lrow);
         if (a.d_params && tid < (int)(sizeof(quasar_sample_params) / 4))
             cp_async4(smem_u32(&s.nxt_pr) + 4u * tid, reinterpret_cast<const char*>(a.d_params + row) + 4 * tid);
         if (tid == 32 && has_len(a)) cp_async4(smem_u32(&s.nxt_len), a.hist_len + row);
@@ -1257,18 +1276,20 @@ __device__ __forceinline__ bool picks_in_stream(const RowCtx& c, const Row& R) {
 // row with a long history (more ring slots than consumer threads) picks its
 // penalized values up from the ring while it streams (pick_penalized) and
 // needs no staged logit.
-template <bool kPickTma>
-__device__ __forceinline__ RowCtx row_setup(const RowsArgs& a, int row, Row& R, uint32_t* bits, SharedA& s,
+template <bool kPickTma, bool kSplit>
+__device__ __forceinline__ RowCtx row_setup(const RowsArgs& a, int lrow, Row& R, uint32_t* bits, SharedA& s,
                                             int& my_id, bool staged) {
     const int tid = threadIdx.x;
     if (staged) {
         cp_async_wait_all();
         csync();  // every thread's copies have landed
     }
+    const int row = state_row<kSplit>(a, lrow);
     const quasar_sample_params pr = a.d_params ? (staged ? s.nxt_pr : a.d_params[row]) : a.h_params;
     const int len_raw = staged ? (has_len(a) ? s.nxt_len : a.hist_cap) : ring_len_raw(a, row);
     const int head_raw = staged ? (has_head(a) ? s.nxt_head : 0) : ring_head_raw(a, row);
-    const RowCtx c = row_ctx_raw(a, row, pr, len_raw, head_raw, R);
+    RowCtx c = row_ctx_raw(a, row, pr, len_raw, head_raw, R);
+    if constexpr (kSplit) split_shard(a, lrow, row, c, R);
     my_id = -1;
     if (R.use_pen) {
         for (int p = tid; p < c.cap; p += CONSUMERS) {
@@ -1510,7 +1531,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
     const uint8_t* bits8 = reinterpret_cast<const uint8_t*>(bits);
     Row R;
     int my_id;
-    const RowCtx c = row_setup<Src::kPick>(a, row, R, bits, s, my_id, staged);
+    const RowCtx c = row_setup<Src::kPick, Src::kSplit>(a, row, R, bits, s, my_id, staged);
     const bool pick = Src::kPick && picks_in_stream(c, R);
     const RowParams& P = c.P;
     src.begin(R);
@@ -1547,7 +1568,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
                 }
             });
         }
-        stage_next_row(a, row + (int)gridDim.x, s);  // s.tfmax is free again
+        stage_next_row<Src::kSplit>(a, row + (int)gridDim.x, s);  // s.tfmax is free again
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const float ov = __shfl_xor_sync(FULL, bv, o);
@@ -1725,7 +1746,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
             }
         });
     }
-    stage_next_row(a, row + (int)gridDim.x, s);  // s.tfmax is free again
+    stage_next_row<Src::kSplit>(a, row + (int)gridDim.x, s);  // s.tfmax is free again
     a.work_tfmax[(int64_t)row * CONSUMERS + tid] = m;
     {
         // anchor deficits, four per word (tbl_off), stored as whole words;
@@ -1760,17 +1781,117 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
 
 // Global max M and inv = (float)(1/sum) of a row split into vocab shards,
 // from the shards' (max, sum against that max) pairs - the same combination
-// as the one over threads inside a shard.
-__device__ __forceinline__ void shard_norm(const RowsArgs& a, int row, float& M, float& inv) {
+// as the one over threads inside a shard. nb: rows per shard in all_stats
+// ([G][nb]). Called by whole warps: the lanes read the shards' pairs
+// together and combine them by butterfly reductions, which leave the same
+// bits in every lane (each step adds the same two values), so every kernel
+// and rank that combines a row's pairs gets the same M and inv.
+__device__ __forceinline__ void shard_norm(const RowsArgs& a, int row, int nb, float& M, float& inv) {
+    const int lane = threadIdx.x & 31;
     float mx = -INFINITY;
-    for (int g = 0; g < a.shard_G; g++) mx = fmaxf(mx, a.all_stats[(int64_t)g * a.B + row].max);
+    for (int g = lane; g < a.shard_G; g += 32) mx = fmaxf(mx, a.all_stats[(int64_t)g * nb + row].max);
+    mx = warp_max(mx);
     double S = 0.0;
-    for (int g = 0; g < a.shard_G; g++) {
-        const quasar_shard_stat st = a.all_stats[(int64_t)g * a.B + row];
+    for (int g = lane; g < a.shard_G; g += 32) {
+        const quasar_shard_stat st = a.all_stats[(int64_t)g * nb + row];
         if (st.max > -INFINITY) S += st.sum * exp((double)st.max - (double)mx);
     }
+    S = warp_sum(S);
     M = mx;
     inv = __double2float_rn(1.0 / S);
+}
+
+// The exact top-k of a vocab shard, for a row whose bound let more elements
+// through than its candidate buffer holds (the k-th largest per-thread
+// maximum bounds the shard's top k loosely when k is near the thread count,
+// or when many elements tie): the k-th largest key (p desc, global id asc)
+// over every element of the shard's 30-nat window is found by a radix
+// select (eight passes of 8 bits over the 64-bit keys, p recomputed in each
+// pass), and the n = min(k, window elements) elements whose keys reach it
+// are written as (scaled value bits, column) entries, unordered, to
+// raw[0, n) (end = 0) or raw[end - n, end). Returns n. One warp; hist: 256
+// words of shared memory apart from raw. Rare (a slow path of one warp over
+// the whole shard).
+__device__ __noinline__ int shard_topk_exact(const Row& R, const uint32_t* bits, const int2* pen, int npen,
+                                             int64_t col0, int k, uint64_t* raw, int end, uint32_t* hist) {
+    const int lane = threadIdx.x & 31;
+    // every window element once: penalized columns with their listed values
+    auto each = [&](auto&& f) {
+        for (int e = lane; e < R.V; e += 32) {
+            if ((bits[e >> 5] >> (e & 31)) & 1u) continue;
+            const float sc = __fmul_rn(__ldg(R.ptr + e), R.inv_t);  // sample.c:142
+            if (sc >= R.thr) f(sc, e);
+        }
+        for (int i = lane; i < npen; i += 32) {
+            const int2 pe = pen[i];
+            const float sc = __int_as_float(pe.y);
+            if (pe.x >= 0 && pe.x < R.V && sc >= R.thr) f(sc, pe.x);
+        }
+    };
+    auto key_of = [&](float sc, int e) {
+        return ((uint64_t)p_key(sc, R.M, R.thr, R.inv) << 32) | (uint32_t)(~(uint32_t)(col0 + e));
+    };
+    uint64_t prefix = 0ull;
+    uint32_t need = (uint32_t)k;  // rank of the wanted key among those matching prefix
+    int n = k;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+        for (int i = lane; i < 256; i += 32) hist[i] = 0u;
+        __syncwarp();
+        const uint64_t hi = shift == 56 ? 0ull : ~0ull << (shift + 8);
+        each([&](float sc, int e) {
+            const uint64_t key = key_of(sc, e);
+            if ((key & hi) == prefix) atomicAdd(&hist[(uint32_t)(key >> shift) & 255u], 1u);
+        });
+        __syncwarp();
+        // bins in descending order, eight per lane: lane l holds 255 - 8l - j
+        uint32_t c[8], t = 0u;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            c[j] = hist[255 - 8 * lane - j];
+            t += c[j];
+        }
+        const uint32_t incl = warp_incl_scan(t, lane), excl = incl - t;
+        if (shift == 56) {
+            const int total = (int)__shfl_sync(FULL, incl, 31);  // window elements
+            if (total <= k) {  // all of them (prefix 0: every key)
+                n = total;
+                __syncwarp();
+                break;
+            }
+        }
+        const bool mine = excl < need && incl >= need;
+        int bin = 0;
+        uint32_t above = 0u;
+        if (mine) {
+            uint32_t acc = excl;
+            for (int j = 0; j < 8; j++) {
+                if (acc + c[j] >= need) {
+                    bin = 255 - 8 * lane - j;
+                    above = acc;
+                    break;
+                }
+                acc += c[j];
+            }
+        }
+        const int src = max(__ffs(__ballot_sync(FULL, mine)) - 1, 0);
+        bin = __shfl_sync(FULL, bin, src);
+        above = __shfl_sync(FULL, above, src);
+        prefix |= (uint64_t)bin << shift;
+        need -= above;
+        __syncwarp();
+    }
+    // the keys at or above the k-th (keys are distinct: exactly n)
+    uint64_t* out = raw + (end > 0 ? end - n : 0);
+    if (lane == 0) hist[0] = 0u;
+    __syncwarp();
+    each([&](float sc, int e) {
+        if (key_of(sc, e) >= prefix) {
+            const uint32_t pos = atomicAdd(&hist[0], 1u);
+            if (pos < (uint32_t)n) out[pos] = ((uint64_t)__float_as_uint(sc) << 32) | (uint32_t)e;
+        }
+    });
+    __syncwarp();
+    return n;
 }
 
 // kLongPen: histories longer than CONSUMERS slots (a separate kernel
@@ -1812,7 +1933,8 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
         // greedy: finished by kernel A; a shard contributes its best column
         if (shard && tid == 0) {
             const quasar_shard_stat st = a.all_stats[(int64_t)a.shard_rank * a.B + row];
-            cand[0] = st.best >= 0 ? ((uint64_t)ord_key(st.max) << 32) | (uint32_t)(~(uint32_t)(a.col0 + st.best))
+            cand[0] = aborted ? SHARD_OVERFLOW
+                    : st.best >= 0 ? ((uint64_t)ord_key(st.max) << 32) | (uint32_t)(~(uint32_t)(a.col0 + st.best))
                                    : 0ull;
             for (int i = 1; i < a.shard_k; i++) cand[i] = 0ull;
         }
@@ -1823,7 +1945,7 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
     for (int i = tid; i < a.nwords; i += CONSUMERS) bits[i] = 0u;
     R.M = info.x;
     R.inv = info.y;
-    if (shard) shard_norm(a, row, R.M, R.inv);  // the row's global max and 1/sum
+    if (shard) shard_norm(a, row, a.B, R.M, R.inv);  // the row's global max and 1/sum
     R.thr = __fsub_rn(R.M, 30.0f);
     // (an aborted kernel A leaves stale summaries: keep every index in range)
     const int npen = min(max(__float_as_int(info.z), 0), a.hist_cap);
@@ -2025,6 +2147,18 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
             rank_cuts(buf, nk, R, P, by_minp ? __fmul_rn(P.min_p, R.inv) : 0.0f, u, s, cand, a.shard_k, a.col0);
             done = true;
             path = QUASAR_PATH_CANDIDATE;
+        } else if (shard && shard_topk && nk > room) {
+            // more survivors than the buffer holds: the shard's exact top_k
+            // (warp 0; raw entries at the top of buf, where rank_cuts reads them)
+            if (tid < 32) {
+                const int n = shard_topk_exact(R, bits, pen_staged ? pen_s : pen, npen, a.col0, P.top_k, buf, CAP,
+                                               reinterpret_cast<uint32_t*>(bk));
+                if (tid == 0) s.ncand = n;
+            }
+            csync();
+            rank_cuts(buf, s.ncand, R, P, 0.0f, u, s, cand, a.shard_k, a.col0);
+            done = true;
+            path = QUASAR_PATH_CANDIDATE;
         } else if (nk > 0 && nk <= room) {
             const uint64_t* keys = buf;
             // raw entries live in buf[CAP - nk, CAP)
@@ -2071,6 +2205,7 @@ __device__ __forceinline__ void finish_row(const RowsArgs& a, int row, uint64_t*
         // merge reports id -1 for it)
         if (!done)
             for (int i = tid; i < a.shard_k; i += CONSUMERS) cand[i] = 0ull;
+        if (aborted) cand[0] = SHARD_OVERFLOW;  // (tid 0) stale summaries: the merge reports id -1
         return;
     }
     if (!done) {
@@ -2099,7 +2234,7 @@ __global__ void __launch_bounds__(CONSUMERS, QS_A_CTAS) sample_rows_ldg(RowsArgs
     for (int row = blockIdx.x; row < a.B; row += gridDim.x) stream_row(a, row, src, bits, anc_s, s, row != (int)blockIdx.x);
 }
 
-template <bool kPickable>
+template <bool kPickable, bool kSplit>
 __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a) {
     extern __shared__ __align__(128) unsigned char dyn[];
     // the ring starts on a 64-byte boundary (the chunk swizzle flips address
@@ -2130,7 +2265,9 @@ __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a)
         const int64_t row_bytes = (int64_t)a.V * 4;
         uint32_t g = 0;
         for (int row = blockIdx.x; row < a.B; row += gridDim.x) {
-            const char* src = reinterpret_cast<const char*>(a.logits + (int64_t)row * a.ld);
+            const float* rp = kSplit ? a.logits + (int64_t)(row % a.split_B) * a.ld + (int64_t)(row / a.split_B) * a.V
+                                     : a.logits + (int64_t)row * a.ld;
+            const char* src = reinterpret_cast<const char*>(rp);
             for (int c = 0; c < ntiles; c++, g++) {
                 const int st = (int)(g % NSTAGE);
                 if (g >= (uint32_t)NSTAGE) {
@@ -2148,7 +2285,7 @@ __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a)
         }
         return;
     }
-    TmaSource<kPickable> src;
+    TmaSource<kPickable, kSplit> src;
     src.ring_u32 = smem_u32(ring);
     src.thr_off = 64u * threadIdx.x + 16u * chunk_swz(threadIdx.x);
     src.full0 = full0;
@@ -2236,17 +2373,31 @@ __global__ void __launch_bounds__(32 * SW_WARPS) sample_rows_shard_cand_warp(Row
     sm.thr = reinterpret_cast<uint16_t*>(base + (size_t)SW_CAP * 8);
     sm.bits = reinterpret_cast<uint32_t*>(base + (size_t)SW_CAP * 8 + CONSUMERS * 2);
     const int k = a.shard_k;
+    const bool split = a.split_B > 0;
+    const int nb = split ? a.split_B : a.B;  // rows per shard in all_stats
+    // an aborted kernel A (bulk-copy ring timeout) left stale summaries: every
+    // row sends the overflow mark, so the merge reports id -1
+    const bool aborted = *reinterpret_cast<volatile int*>(a.work_abort) != 0;
     for (int row = blockIdx.x * SW_WARPS + w; row < a.B; row += gridDim.x * SW_WARPS) {
-        const quasar_sample_params pr = a.d_params ? a.d_params[row] : a.h_params;
+        const int srow = split ? row % a.split_B : row;
+        const int rank = split ? row / a.split_B : a.shard_rank;
+        const quasar_sample_params pr = a.d_params ? a.d_params[srow] : a.h_params;
         Row R;
-        const RowCtx c = row_ctx(a, row, pr, R);
+        RowCtx c = row_ctx(a, srow, pr, R);
+        if (split) split_shard(a, row, srow, c, R);
+        const int64_t col0 = c.col0;
         const RowParams& P = c.P;
         uint64_t* out = a.shard_cand + (int64_t)row * k;
+        if (aborted) {
+            for (int i = lane; i < k; i += 32) out[i] = i == 0 ? SHARD_OVERFLOW : 0ull;
+            __syncwarp();
+            continue;
+        }
         if (!(pr.temperature > 0.0f)) {
             // greedy: this shard's best column (kernel A), as in the CTA kernel
             if (lane == 0) {
-                const quasar_shard_stat st = a.all_stats[(int64_t)a.shard_rank * a.B + row];
-                out[0] = st.best >= 0 ? ((uint64_t)ord_key(st.max) << 32) | (uint32_t)(~(uint32_t)(a.col0 + st.best))
+                const quasar_shard_stat st = a.all_stats[(int64_t)rank * nb + srow];
+                out[0] = st.best >= 0 ? ((uint64_t)ord_key(st.max) << 32) | (uint32_t)(~(uint32_t)(col0 + st.best))
                                       : 0ull;
             }
             for (int i = 1 + lane; i < k; i += 32) out[i] = 0ull;
@@ -2264,7 +2415,7 @@ __global__ void __launch_bounds__(32 * SW_WARPS) sample_rows_shard_cand_warp(Row
         }
         const float4 info = a.work_info[row];
         const int npen = min(max(__float_as_int(info.z), 0), a.hist_cap);
-        shard_norm(a, row, R.M, R.inv);  // the row's global max and 1/sum
+        shard_norm(a, srow, nb, R.M, R.inv);  // the row's global max and 1/sum
         R.thr = __fsub_rn(R.M, 30.0f);
         const float* tf = a.work_tfmax + (int64_t)row * CONSUMERS;
         float lo = -INFINITY;
@@ -2379,6 +2530,9 @@ __global__ void __launch_bounds__(32 * SW_WARPS) sample_rows_shard_cand_warp(Row
             ncand += __popc(bal);
         }
         __syncwarp();
+        if (shard_topk && ncand > SW_CAP)  // the bound let too many through: the shard's exact top_k
+            ncand = shard_topk_exact(R, sm.bits, pen, npen, col0, P.top_k, sm.cand, 0,
+                                     reinterpret_cast<uint32_t*>(sm.cand + SW_CAP / 2));
         if (ncand > SW_CAP || (!shard_topk && ncand > k)) {
             // more candidates than this shard can hold or send
             for (int i = lane; i < k; i += 32) out[i] = i == 0 ? SHARD_OVERFLOW : 0ull;
@@ -2391,7 +2545,7 @@ __global__ void __launch_bounds__(32 * SW_WARPS) sample_rows_shard_cand_warp(Row
         for (int i = lane; i < ncand; i += 32) {
             const uint64_t en = sm.cand[i];
             const uint32_t pk = p_key(__uint_as_float((uint32_t)(en >> 32)), R.M, R.thr, R.inv);
-            sm.cand[i] = ((uint64_t)pk << 32) | (uint32_t)(~(uint32_t)(a.col0 + (int64_t)(uint32_t)en));
+            sm.cand[i] = ((uint64_t)pk << 32) | (uint32_t)(~(uint32_t)(col0 + (int64_t)(uint32_t)en));
         }
         __syncwarp();
         constexpr int PER = 4;  // keys a lane ranks per sweep
@@ -2459,12 +2613,15 @@ __global__ void __launch_bounds__(256) sample_rows_merge_warp(RowsArgs a) {
         if (!(pr.temperature > 0.0f)) {
             // greedy: the largest penalized logit over the shards, lowest
             // global id on ties (sample.c:130-134)
-            if (lane == 0) write_row(a, row, c, nk > 0 ? (int)(~(uint32_t)best) : 0, 0, 1.0f, 0.0f, QUASAR_PATH_GREEDY, 0ull);
+            // (overflow: a shard's streaming pass aborted - id -1)
+            if (lane == 0)
+                write_row(a, row, c, overflow ? -1 : nk > 0 ? (int)(~(uint32_t)best) : 0, 0, 1.0f, 0.0f,
+                          QUASAR_PATH_GREEDY, 0ull);
             __syncwarp();
             continue;
         }
         float M = 0.0f, inv = 0.0f;
-        shard_norm(a, row, M, inv);
+        shard_norm(a, row, a.B, M, inv);
         uint64_t st_rng = a.rng[row];
         const double u = rng_unit(&st_rng);  // sample.c:173: one step per stochastic row
         int id = -1, nc = 0;
@@ -2573,11 +2730,12 @@ __global__ void __launch_bounds__(CONSUMERS, 3) sample_rows_merge(RowsArgs a) {
         // a shard that overflowed its min-p keys (the largest key sorts first)
         const bool overflow = nk > 0 && buf[0] == SHARD_OVERFLOW;
         if (!(pr.temperature > 0.0f)) {
-            if (tid == 0)
-                write_row(a, row, c, nk > 0 ? (int)(~(uint32_t)buf[0]) : 0, 0, 1.0f, 0.0f, QUASAR_PATH_GREEDY, 0ull);
+            if (tid == 0)  // (overflow: a shard's streaming pass aborted - id -1)
+                write_row(a, row, c, overflow ? -1 : nk > 0 ? (int)(~(uint32_t)buf[0]) : 0, 0, 1.0f, 0.0f,
+                          QUASAR_PATH_GREEDY, 0ull);
         } else {
             float M, inv;
-            shard_norm(a, row, M, inv);
+            shard_norm(a, row, a.B, M, inv);
             uint64_t st_rng = a.rng[row];
             const double u = rng_unit(&st_rng);  // sample.c:173
             if (nk > 0 && !overflow) {
@@ -2630,8 +2788,8 @@ struct KernelCfg {
     std::atomic<size_t> smem_set[64];
     std::atomic<int> grid[64];  // resident CTAs of the kernel on each device
 };
-KernelCfg g_ldg, g_tma, g_tma_pick, g_fin, g_fin_long, g_fin_shard, g_fin_shard_long, g_merge, g_merge_warp,
-    g_shard_warp;
+KernelCfg g_ldg, g_tma, g_tma_pick, g_tma_split, g_tma_pick_split, g_fin, g_fin_long, g_fin_shard,
+    g_fin_shard_long, g_merge, g_merge_warp, g_shard_warp;
 std::mutex g_cfg_mu;
 
 cudaError_t configure(KernelCfg& cfg, const void* fn, int threads, size_t smem, int dev, int& grid) {
@@ -2692,15 +2850,19 @@ cudaError_t launch_stream(const RowsArgs& a, int dev, cudaStream_t stream) {
     if (a.tma) {
         const size_t smem = rows_tma_smem_bytes(a.V);
         int grid = 0;
-        if (a.hist && a.hist_cap > rows::CONSUMERS) {  // long histories: penalized values picked up in the stream
-            err = configure(g_tma_pick, (const void*)rows::sample_rows_tma<true>, rows::CONSUMERS + 32, smem, dev, grid);
-            if (err != cudaSuccess) return err;
-            rows::sample_rows_tma<true><<<min(a.B, grid), rows::CONSUMERS + 32, smem, stream>>>(a);
-        } else {
-            err = configure(g_tma, (const void*)rows::sample_rows_tma<false>, rows::CONSUMERS + 32, smem, dev, grid);
-            if (err != cudaSuccess) return err;
-            rows::sample_rows_tma<false><<<min(a.B, grid), rows::CONSUMERS + 32, smem, stream>>>(a);
-        }
+        // long histories: penalized values picked up in the stream; split
+        // launches: launch rows are column shards (an instance each)
+        const bool pick = a.hist && a.hist_cap > rows::CONSUMERS, split = a.split_B > 0;
+        const void* fn = split ? (pick ? (const void*)rows::sample_rows_tma<true, true>
+                                       : (const void*)rows::sample_rows_tma<false, true>)
+                               : (pick ? (const void*)rows::sample_rows_tma<true, false>
+                                       : (const void*)rows::sample_rows_tma<false, false>);
+        KernelCfg& cfg = split ? (pick ? g_tma_pick_split : g_tma_split) : (pick ? g_tma_pick : g_tma);
+        err = configure(cfg, fn, rows::CONSUMERS + 32, smem, dev, grid);
+        if (err != cudaSuccess) return err;
+        void* args[] = {const_cast<RowsArgs*>(&a)};
+        err = cudaLaunchKernel(fn, dim3(min(a.B, grid)), dim3(rows::CONSUMERS + 32), args, smem, stream);
+        if (err != cudaSuccess) return err;
     } else {
         const size_t smem = rows_smem_bytes(a.V);
         int grid = 0;
@@ -2708,6 +2870,18 @@ cudaError_t launch_stream(const RowsArgs& a, int dev, cudaStream_t stream) {
         if (err != cudaSuccess) return err;
         rows::sample_rows_ldg<<<min(a.B, grid), rows::CONSUMERS, smem, stream>>>(a);
     }
+    return cudaGetLastError();
+}
+
+// The vocab-shard candidate kernel with one warp per row (V <= SW_MAX_COLS).
+cudaError_t launch_cand_warp(const RowsArgs& a, int dev, cudaStream_t stream) {
+    const size_t smem = rows::SW_WARPS * rows::sw_warp_bytes(a.V);
+    int grid = 0;
+    cudaError_t err =
+        configure(g_shard_warp, (const void*)rows::sample_rows_shard_cand_warp, 32 * rows::SW_WARPS, smem, dev, grid);
+    if (err != cudaSuccess) return err;
+    const int ctas = min((a.B + rows::SW_WARPS - 1) / rows::SW_WARPS, grid);
+    rows::sample_rows_shard_cand_warp<<<ctas, 32 * rows::SW_WARPS, smem, stream>>>(a);
     return cudaGetLastError();
 }
 
@@ -2758,16 +2932,7 @@ cudaError_t launch_shard_candidates(const RowsArgs& args, void* workspace, cudaS
     int dev = 0;
     cudaError_t err = current_device(dev);
     if (err != cudaSuccess) return err;
-    if (a.V <= rows::SW_MAX_COLS) {  // one warp per row
-        const size_t smem = rows::SW_WARPS * rows::sw_warp_bytes(a.V);
-        int grid = 0;
-        err = configure(g_shard_warp, (const void*)rows::sample_rows_shard_cand_warp, 32 * rows::SW_WARPS, smem, dev,
-                        grid);
-        if (err != cudaSuccess) return err;
-        const int ctas = min((a.B + rows::SW_WARPS - 1) / rows::SW_WARPS, grid);
-        rows::sample_rows_shard_cand_warp<<<ctas, 32 * rows::SW_WARPS, smem, stream>>>(a);
-        return cudaGetLastError();
-    }
+    if (a.V <= rows::SW_MAX_COLS) return launch_cand_warp(a, dev, stream);  // one warp per row
     return launch_finish(a, dev, stream);
 }
 
@@ -2777,14 +2942,19 @@ size_t rows_merge_smem_bytes(int G, int k) {
     return n2 * sizeof(uint64_t);
 }
 
+constexpr int MERGE_WARP_MIN_ROWS = 256;
+
 cudaError_t launch_shard_merge(const RowsArgs& args, cudaStream_t stream) {
     int dev = 0;
     cudaError_t err = current_device(dev);
     if (err != cudaSuccess) return err;
-    // one warp per row while a warp's keys fit: up to 8 warps per CTA within
-    // 96 KB of shared memory
+    // one warp per row while a warp's keys fit (up to 8 warps per CTA within
+    // 96 KB of shared memory) and the batch is large enough to keep the SMs
+    // busy with warps; a small batch gets one CTA per row (its sort has 8
+    // times the threads of a warp's binary searches: a one-row merge of 32
+    // shards' 20 keys took 213 us on one warp)
     const size_t per_warp = (size_t)16 * args.shard_G * args.shard_k;
-    if (per_warp <= (size_t)96 * 1024) {
+    if (per_warp <= (size_t)96 * 1024 && args.B >= MERGE_WARP_MIN_ROWS) {
         int warps = (int)min((size_t)8, (size_t)96 * 1024 / per_warp);
         const size_t wsmem = per_warp * warps;
         int grid = 0;
@@ -2800,6 +2970,110 @@ cudaError_t launch_shard_merge(const RowsArgs& args, cudaStream_t stream) {
     if (err != cudaSuccess) return err;
     rows::sample_rows_merge<<<min(args.B, grid), rows::CONSUMERS, smem, stream>>>(args);
     return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Split rows. With B rows the streaming kernel runs B CTAs (one per row), so
+// a small batch uses a few of the 148 SMs and its latency is one SM's
+// bandwidth over a whole row (~15 us for 608 KB). A small batch whose
+// parameters are on the host is instead streamed as G column shards per row
+// (G * B CTAs) by the streaming kernel's split instance, and finished by the
+// vocab-shard candidate kernel (one warp per shard row: the shard's top-k
+// keys against the row's global max and sum) and the shard merge kernel
+// (cuts and draw over the G * k keys, PRNG step, ring append) - the
+// three-phase vocab-sharded pick of one GPU, with the all-gathers done by
+// placement. Exact for greedy rows and for rows with 1 <= top_k <= 256 (every
+// kept element is among some shard's top_k); other rows stay on the one-CTA
+// path, where the candidate path's min-p bound or the exact select applies.
+#ifndef QS_SPLIT_MAX_G
+#define QS_SPLIT_MAX_G 8     // shards per row at most (16 and 32 were slower: the merge grows with G)
+#endif
+#ifndef QS_SPLIT_MAX_ROWS
+#define QS_SPLIT_MAX_ROWS 256  // shard rows (CTAs of the streaming kernel) per launch at most
+#endif
+#ifndef QS_SPLIT_MIN_COLS
+#define QS_SPLIT_MIN_COLS 2048  // columns per shard at least
+#endif
+// workspace of a split launch at most (long histories make the shard rows'
+// penalized lists large; such batches take the one-CTA path instead)
+constexpr size_t SPLIT_MAX_WS = (size_t)16 << 20;
+
+namespace {
+size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
+}  // namespace
+
+int split_shards(const RowsArgs& a) {
+    if (a.B < 1 || a.B > SPLIT_MAX_B || a.d_params || !a.tma) return 0;
+    if (a.flags & (QUASAR_FLAG_EXACT_SELECT | QUASAR_FLAG_NO_SPLIT)) return 0;
+    const quasar_sample_params& p = a.h_params;
+    if (p.temperature > 0.0f && !(p.top_k >= 1 && p.top_k <= SPLIT_MAX_K)) return 0;
+    // the workspace of the most shards B rows can get within SPLIT_MAX_WS (so
+    // a workspace of quasar_sampler_workspace_bytes covers any G chosen here)
+    if (split_workspace_bytes(a.B, 0, a.hist ? a.hist_cap : 0) == 0) return 0;
+    // the most shards whose columns stay a multiple of 4 (16-byte aligned
+    // bulk copies) and fit the one-warp candidate kernel
+    for (int G = QS_SPLIT_MAX_G; G >= 2; G >>= 1) {
+        const int vs = a.V / G;
+        if (a.V % G != 0 || vs % 4 != 0 || vs < QS_SPLIT_MIN_COLS || vs > rows::SW_MAX_COLS) continue;
+        if (G * a.B > QS_SPLIT_MAX_ROWS) continue;
+        return G;
+    }
+    return 0;
+}
+
+// [summaries of G*B shard rows (rows_workspace_bytes)][stats [G][B]][keys [G][B][k]].
+// G <= 0: the most shards a batch of B rows can be given (any V); 0 when that
+// exceeds SPLIT_MAX_WS (the batch is never split).
+size_t split_workspace_bytes(int B, int G, int hist_cap) {
+    if (B < 1 || B > SPLIT_MAX_B) return 0;
+    const bool largest = G <= 0;
+    if (largest)
+        for (G = QS_SPLIT_MAX_G; G > 2 && G * B > QS_SPLIT_MAX_ROWS; G >>= 1) {
+        }
+    const size_t R = (size_t)B * (size_t)G;
+    const size_t bytes = align256(rows_workspace_bytes((int)R, hist_cap)) +
+                         align256(R * sizeof(quasar_shard_stat)) + R * SPLIT_MAX_K * sizeof(uint64_t);
+    return largest && bytes > SPLIT_MAX_WS ? 0 : bytes;
+}
+
+cudaError_t launch_split_rows(const RowsArgs& args, int G, void* workspace, cudaStream_t stream) {
+    int dev = 0;
+    cudaError_t err = current_device(dev);
+    if (err != cudaSuccess) return err;
+    const int B = args.B, R = B * G, k = args.h_params.temperature > 0.0f ? args.h_params.top_k : 1;
+    char* ws = reinterpret_cast<char*>(workspace);
+    const size_t rows_bytes = align256(rows_workspace_bytes(R, args.hist ? args.hist_cap : 0));
+    quasar_shard_stat* stats = reinterpret_cast<quasar_shard_stat*>(ws + rows_bytes);
+    uint64_t* cand = reinterpret_cast<uint64_t*>(ws + rows_bytes + align256((size_t)R * sizeof(quasar_shard_stat)));
+    // phase 1: every shard row streamed once, its (max, sum, best) published
+    RowsArgs a = args;
+    a.B = R;
+    a.V = args.V / G;
+    a.split_B = B;
+    a.vec = args.vec && a.V % 8 == 0;  // shard starts 32-byte aligned
+    a.record = 0;
+    a.out = nullptr;
+    a.diag = nullptr;
+    layout_workspace(a, workspace);
+    a.shard_stats = stats;
+    err = launch_stream(a, dev, stream);
+    if (err != cudaSuccess) return err;
+    // phase 2: each shard row's top-k keys against the row's global max and sum
+    a.shard_stats = nullptr;
+    a.all_stats = stats;
+    a.shard_G = G;
+    a.shard_k = k;
+    a.shard_rank = 0;
+    a.shard_cand = cand;
+    err = launch_cand_warp(a, dev, stream);
+    if (err != cudaSuccess) return err;
+    // phase 3: the B rows' cuts, draws, PRNG steps and ring appends
+    RowsArgs m = args;
+    m.all_stats = stats;
+    m.shard_G = G;
+    m.shard_k = k;
+    m.shard_cand = cand;
+    return launch_shard_merge(m, stream);
 }
 
 }  // namespace qs

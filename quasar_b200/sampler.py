@@ -141,6 +141,27 @@ def pick_batch(logits, rng, *, params=None, d_params=None, hist=None, hist_len=N
     return out
 
 
+def split_shards(B: int, V: int, *, params=None, per_row_params: bool = False, hist_cap: int = 0, flags: int = 0,
+                 ld: int = None, ptr: int = 256) -> int:
+    """Column shards per row that pick_batch streams a batch of B rows in (0: one CTA per row).
+
+    params: the record shared by all rows (as pick_batch's ``params``);
+    per_row_params: the rows have device parameters instead (never split).
+    ptr / ld: the logits address and row stride the call would get (the
+    bulk-copy alignment conditions). Host arithmetic only, no GPU call."""
+    hp = None
+    if not per_row_params:
+        if isinstance(params, dict):
+            params = make_params(1, **params)
+        rec = np.asarray(params, dtype=PARAMS_DTYPE).reshape(-1)[0]
+        hp = SampleParams(float(rec["temperature"]), float(rec["top_p"]), float(rec["min_p"]),
+                          float(rec["repeat_penalty"]), int(rec["top_k"]), 0)
+    return int(lib().quasar_sampler_split_shards(
+        ctypes.c_void_p(ptr), int(V if ld is None else ld), int(B), int(V),
+        ctypes.c_void_p(16) if per_row_params else None, None if hp is None else ctypes.byref(hp),
+        int(hist_cap), int(flags)))
+
+
 def workspace_bytes(B: int, hist_cap: int = 0) -> int:
     """Bytes of device workspace one pick_batch call over B rows with history capacity hist_cap needs."""
     return int(lib().quasar_sampler_workspace_bytes(int(B), int(hist_cap)))
@@ -172,5 +193,5 @@ def synth_uniform(seed: int, row0: int, B: int, lo: float, hi: float, out, strea
 
 
 __all__ = ["Sampler", "SampleParams", "make_params", "params_to_device", "pick_batch", "workspace_bytes",
-           "synth_logits", "synth_hist", "synth_uniform", "PARAMS_DTYPE", "DIAG_DTYPE",
+           "split_shards", "synth_logits", "synth_hist", "synth_uniform", "PARAMS_DTYPE", "DIAG_DTYPE",
            "FLAG_EXACT_SELECT"]

@@ -213,3 +213,30 @@ def test_emulated_shards_min_p_rows_without_top_k(G):
                                hist_len=hist_len[keep], hist_head=hist_head[keep])
     assert_parity(ids[keep], diag[keep].view(q.DIAG_DTYPE).reshape(-1), rng[keep].view(np.uint64), ref, ref_rng)
     assert (ids[keep] >= 0).all()
+
+
+@pytest.mark.parametrize("G", [2, 8])
+def test_emulated_shards_top_k_rows_whose_bound_overflows(G):
+    """Top-k rows whose per-thread-maxima bound lets more elements through a
+    shard than its candidate buffer holds (the one-warp kernel at G = 8 holds
+    512, the CTA kernel at G = 2 holds 4096): logits quantised to 7 values,
+    so every thread's maximum ties and a shard holds thousands of elements at
+    the row maximum, and flat rows with top_k = 256. Each shard then finds
+    its exact top k by a radix select over the whole shard; ties go to the
+    lowest ids, as the reference's sort leaves them."""
+    import torch
+    import quasar_b200 as q
+    nb = 8
+    base = torch.randint(-3, 4, (nb, V_FULL), generator=torch.Generator().manual_seed(5)).float()
+    logits = base.cuda()
+    hist = torch.randint(0, V_FULL, (nb, H), generator=torch.Generator().manual_seed(6)).int().cuda()
+    prm = O.make_params(nb, temperature=1.0, top_k=40, top_p=0.95, repeat_penalty=1.2)
+    prm["top_k"][1::2] = 256
+    prm["temperature"][1::2] = 3.0   # flat rows: the top 256 are ties and near-ties
+    prm["min_p"][2::4] = 0.5
+    seeds, hist_len, hist_head = _state(nb)
+    ids, diag, rng, th, tl = _emulate(logits, hist, prm, seeds, hist_len, hist_head, G, k=256)
+    ref, ref_rng = O.pick_rows(base.numpy(), prm, seeds, hist=hist.cpu().numpy(), hist_len=hist_len.copy(),
+                               hist_head=hist_head.copy())
+    assert (ids >= 0).all(), ids
+    assert_parity(ids, diag.view(q.DIAG_DTYPE).reshape(-1), rng.view(np.uint64), ref, ref_rng, max_mismatch_frac=0.0)
