@@ -385,7 +385,8 @@ def run_latency(args) -> None:
     call: each call blocks until the id is on the host), and
     quasar_sampler_pick_batch with B=1 on device-resident state (CUDA events
     over back-to-back calls), the last also at B = 4 and 16 and with each
-    row on one CTA (QUASAR_FLAG_NO_SPLIT) beside the default column split.
+    row on one CTA (QUASAR_FLAG_NO_SPLIT) beside the default fused cluster
+    kernel of small batches.
     The reference sample.c, one core, on the same row is the CPU figure."""
     import torch
     import quasar_b200 as q
@@ -465,7 +466,7 @@ def run_latency(args) -> None:
                            "pick_batch_B1_device_per_call": batch_ms1, **small},
             "split_shards_B1": q.split_shards(1, V, params=prm, hist_cap=64),
             "e2e": {"value": host_ms, "unit": "ms", "h2d_bytes_per_step": V * 4, "d2h_bytes_per_step": 4},
-            "gpu_launches": steps * (3 if q.split_shards(1, V, params=prm, hist_cap=64) else 2),
+            "gpu_launches": steps * (1 if q.split_shards(1, V, params=prm, hist_cap=64) else 2),
             "cpu_baseline": {"value": ref_ms, "unit": "ms", "cores": 1, "kind": "reference",
                              "sample": f"{n_ref} picks of the same row through one reference sampler object"}}
     print(json.dumps(line), flush=True)

@@ -108,8 +108,9 @@ typedef struct {
                                         results) */
 #define QUASAR_FLAG_NO_SPLIT      4  /* stream every row on one CTA, also for
                                         the small batches that are otherwise
-                                        split into column shards (same ids
-                                        within the stochastic tolerance) */
+                                        sampled by a cluster of CTAs per row
+                                        (same ids within the stochastic
+                                        tolerance) */
 
 /* Sample B rows of d_logits (row r at d_logits + r*ld, V columns, fp32).
  *   d_params    [B] per-row parameters on the device, or NULL to use *h_params
@@ -130,11 +131,12 @@ typedef struct {
  * persistent CTAs read them with 256-bit (32-byte aligned rows) or scalar
  * loads. A second kernel finishes the stochastic rows. Small batches
  * (B <= 16) with host parameters (d_params NULL) whose rows are greedy or have
- * 1 <= top_k <= 256 are split instead: each row is streamed as up to 8 column
- * shards by as many CTAs, then the shards' top-k candidates are merged (three
- * launches; the latency case of one row, as quasar_sampler_pick makes it);
- * this needs the workspace size quasar_sampler_workspace_bytes reports and the
- * bulk-copy conditions above, else the rows take the one-CTA path. Finite logits
+ * 1 <= top_k <= 256 take one fused kernel instead (the latency case of one
+ * row, as quasar_sampler_pick makes it): a cluster of 8 CTAs per row, each
+ * holding V/8 columns in shared memory, exchanging the row's max and sum and
+ * its top-k candidates through distributed shared memory; it needs the
+ * bulk-copy conditions above, V % 32 == 0 and V >= 8192 (no workspace is
+ * used). Finite logits
  * only (as in the reference, NaN/inf give unspecified picks). Asynchronous on
  * `stream`; returns after the launch. Replaces, batched, sample.h:29. */
 #define QUASAR_MAX_VOCAB (1 << 20)
@@ -152,8 +154,7 @@ int quasar_sampler_pick_batch(const float *d_logits, int64_t ld, int B, int V,
 /* Device workspace one quasar_sampler_pick_batch call of B rows with history
  * capacity hist_cap needs: the per-row summaries the streaming kernel leaves
  * for the finishing kernel (row max and 1/sum, per-thread maxima, tile-max
- * table, penalized-id list; ~15 KB per row at hist_cap 256; for B <= 16 it
- * also covers the split of each row into 8 column shards). Pass
+ * table, penalized-id list; ~15 KB per row at hist_cap 256). Pass
  * d_workspace = NULL to use a workspace the library allocates and keeps per
  * (device, stream): calls on different streams never share one, and calls on
  * one stream are ordered by it. It grows with stream-ordered allocations
@@ -161,10 +162,10 @@ int quasar_sampler_pick_batch(const float *d_logits, int64_t ld, int B, int V,
  * synchronisation. */
 size_t quasar_sampler_workspace_bytes(int B, int hist_cap);
 
-/* Column shards per row that quasar_sampler_pick_batch, given these arguments
- * and a workspace of quasar_sampler_workspace_bytes(B, hist_cap) bytes (or
- * none), streams each row of the batch in (0: one CTA per row, no split).
- * Host-side arithmetic only: no GPU call, pointers are not dereferenced. */
+/* CTAs per row (the cluster size) of the fused small-batch kernel that
+ * quasar_sampler_pick_batch uses for these arguments (0: the batch takes the
+ * streaming and finishing kernels, one CTA per row). Host-side arithmetic
+ * only: no GPU call, pointers are not dereferenced. */
 int quasar_sampler_split_shards(const float *d_logits, int64_t ld, int B, int V,
                                 const quasar_sample_params *d_params,
                                 const quasar_sample_params *h_params, int hist_cap, int flags);
@@ -172,8 +173,8 @@ int quasar_sampler_split_shards(const float *d_logits, int64_t ld, int B, int V,
 /* Kernel launches one quasar_sampler_pick_batch call makes (2: the streaming
  * kernel, which also finishes greedy rows, and the finishing kernel of the
  * stochastic rows: cuts, exact select where needed, draw), plus one 4-byte
- * memset of the workspace abort word. A split small batch makes 3 (streaming,
- * shard candidates, merge). A row whose id comes
+ * memset of the workspace abort word. A small batch that takes the fused
+ * cluster kernel makes 1 launch and no memset. A row whose id comes
  * back -1 hit the bounded-wait timeout of the bulk-copy ring (a device fault,
  * not a sampling result). */
 int quasar_sampler_pick_batch_launches(void);

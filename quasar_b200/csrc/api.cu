@@ -138,9 +138,8 @@ int sync_config(quasar_sampler* s) {
             return QUASAR_ECUDA;
         s->hist_cap = s->repeat_last_n;
     }
-    // this object's own workspace for a one-row pick with its ring (split
-    // into column shards when its parameters allow)
-    rc = object_workspace(s, quasar_sampler_workspace_bytes(1, s->hist_cap));
+    // this object's own workspace for a one-row pick with its ring
+    rc = object_workspace(s, qs::rows_workspace_bytes(1, s->hist_cap));
     if (rc != QUASAR_OK) return rc;
     if (s->rng_dirty) {
         if (cudaMemcpyAsync(s->d_rng, &s->seed_state, sizeof(uint64_t), cudaMemcpyHostToDevice,
@@ -208,16 +207,11 @@ int quasar_sampler_split_shards(const float* d_logits, int64_t ld, int B, int V,
     a.hist_cap = hist_cap;
     a.flags = flags;
     a.tma = qs::rows_tma_ok(d_logits, ld, V) && !(flags & QUASAR_FLAG_NO_TMA);
-    const int G = qs::split_shards(a);
-    return G > 0 && qs::split_workspace_bytes(B, G, hist_cap) <= quasar_sampler_workspace_bytes(B, hist_cap) ? G : 0;
+    return qs::small_batch_shards(a);
 }
 
 size_t quasar_sampler_workspace_bytes(int B, int hist_cap) {
-    if (B <= 0) return 0;
-    const size_t rows = qs::rows_workspace_bytes(B, hist_cap);
-    if (B > qs::SPLIT_MAX_B) return rows;
-    const size_t split = qs::split_workspace_bytes(B, 0, hist_cap);
-    return split > rows ? split : rows;
+    return B > 0 ? qs::rows_workspace_bytes(B, hist_cap) : 0;
 }
 
 int quasar_sampler_pick_batch(const float* d_logits, int64_t ld, int B, int V,
@@ -250,24 +244,18 @@ int quasar_sampler_pick_batch(const float* d_logits, int64_t ld, int B, int V,
     a.vec = ((uintptr_t)d_logits % 32 == 0) && (ld % 8 == 0);
     a.tma = qs::rows_tma_ok(d_logits, ld, V) && !(flags & QUASAR_FLAG_NO_TMA);
     const cudaStream_t st = (cudaStream_t)stream;
-    // a small batch with host parameters: G column shards per row (0: one CTA per row)
-    const int G = qs::split_shards(a);
-    const size_t split_bytes = G > 0 ? qs::split_workspace_bytes(B, G, hist_cap) : 0;
-    if (d_workspace) {
-        if (workspace_bytes < qs::rows_workspace_bytes(B, hist_cap) || (uintptr_t)d_workspace % 256 != 0)
-            return QUASAR_EINVAL;
-        const cudaError_t err = G > 0 && workspace_bytes >= split_bytes
-                                    ? qs::launch_split_rows(a, G, d_workspace, st)
-                                    : qs::launch_sample_rows(a, d_workspace, st);
-        return err == cudaSuccess ? QUASAR_OK : QUASAR_ECUDA;
-    }
+    if (d_workspace && (workspace_bytes < qs::rows_workspace_bytes(B, hist_cap) || (uintptr_t)d_workspace % 256 != 0))
+        return QUASAR_EINVAL;
+    // a small batch with host parameters: one fused kernel, a cluster of G
+    // CTAs per row (no workspace)
+    const int G = qs::small_batch_shards(a);
+    if (G > 0) return qs::launch_small_batch(a, G, st) == cudaSuccess ? QUASAR_OK : QUASAR_ECUDA;
+    if (d_workspace) return qs::launch_sample_rows(a, d_workspace, st) == cudaSuccess ? QUASAR_OK : QUASAR_ECUDA;
     std::lock_guard<std::mutex> lock(g_ws_mu);  // held until the launch is queued
     void* ws = nullptr;
-    const size_t rows_bytes = qs::rows_workspace_bytes(B, hist_cap);
-    const int wrc = managed_workspace(split_bytes > rows_bytes ? split_bytes : rows_bytes, st, &ws);
+    const int wrc = managed_workspace(qs::rows_workspace_bytes(B, hist_cap), st, &ws);
     if (wrc != QUASAR_OK) return wrc;
-    const cudaError_t err = G > 0 ? qs::launch_split_rows(a, G, ws, st) : qs::launch_sample_rows(a, ws, st);
-    return err == cudaSuccess ? QUASAR_OK : QUASAR_ECUDA;
+    return qs::launch_sample_rows(a, ws, st) == cudaSuccess ? QUASAR_OK : QUASAR_ECUDA;
 }
 
 quasar_sampler* quasar_sampler_new(void) {

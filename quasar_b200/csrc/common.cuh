@@ -218,4 +218,30 @@ __device__ __forceinline__ T warp_incl_scan(T v, int lane) {
     return v;
 }
 
+// exp(x) rounded once to float (through double). Kept out of line: the
+// whole-row passes of the select path call it from unrolled loops, where an
+// inlined copy per element made the kernel's code too large for the
+// instruction cache.
+#ifndef QS_EXP_NOINLINE
+#define QS_EXP_NOINLINE 1
+#endif
+#if QS_EXP_NOINLINE
+static __device__ __noinline__
+#else
+static __device__ __forceinline__
+#endif
+float exp_rounded(float x) {
+    return __double2float_rn(exp((double)x));
+}
+// p key of one penalized, scaled logit: bits of p = (float)exp(sc - M) * inv,
+// 0 outside the window. Every path uses it, so they agree bit for bit. For
+// finite logits p <= 1; the clamp keeps every key that non-finite logits
+// could produce (inf, NaN, negative NaN bits) at or below the key of 1.0f,
+// so keys always index the histograms and buckets in range.
+__device__ __forceinline__ uint32_t p_key(float sc, float M, float thr, float inv) {
+    if (!(sc >= thr)) return 0u;
+    const float e = exp_rounded(__fsub_rn(sc, M));
+    return min(__float_as_uint(__fmul_rn(e, inv)), 0x3F800000u);
+}
+
 }  // namespace qs

@@ -48,6 +48,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "ptx.cuh"
 #include "sample_rows.cuh"
 
 namespace qs {
@@ -85,7 +86,6 @@ constexpr int NB = 1024;                       // radix bins per level (10 bits)
 // Candidate key a vocab shard sends first when it has more min-p survivors
 // than keys to send (no real key reaches it: p keys are at most 1.0f's bits)
 constexpr uint64_t SHARD_OVERFLOW = ~0ull;
-constexpr long long WAIT_CYCLES = 1ll << 32;   // ~2 s: bound on any mbarrier wait
 constexpr float REF_SLACK = 64.0f;             // kernel A: exp reference lag (nats), e^64 << FLT_MAX
 #ifndef QS_LDG_DEPTH
 #define QS_LDG_DEPTH 1
@@ -151,54 +151,11 @@ struct SharedA : Shared {
 // takes part, so it can run ahead into the next row.
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-// ---- mbarrier / bulk-copy primitives (PTX ISA: mbarrier, cp.async.bulk) ----
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait: false after WAIT_CYCLES without the phase completing.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity))
-        if (clock64() - t0 > WAIT_CYCLES) return false;
-    return true;
-}
 __device__ __forceinline__ void lds4(uint32_t addr, float* v) {
     asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
                  : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3])
                  : "r"(addr)
                  : "memory");
-}
-// The logits are read once: their lines are marked first to go from L2, so
-// they do not push out the per-row summaries the finishing kernel reads.
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-    uint64_t pol;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(dst),
-        "l"(src), "r"(bytes), "r"(bar), "l"(pol)
-        : "memory");
 }
 // Asynchronous 4-byte global -> shared copy (cp.async) and its wait.
 __device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
@@ -249,32 +206,6 @@ __device__ __forceinline__ void apply_pen_oct(float* v, uint32_t m, float rp) {
 #pragma unroll
     for (int k = 0; k < 8; k++)
         if (m & (1u << k)) v[k] = penalize(v[k], rp);
-}
-
-// p key of one penalized, scaled logit: bits of p = (float)exp(sc - M) * inv,
-// 0 outside the window. Both paths use it, so they agree bit for bit. For
-// finite logits p <= 1; the clamp keeps every key that non-finite logits
-// could produce (inf, NaN, negative NaN bits) at or below the key of 1.0f,
-// so keys always index the histograms and buckets in range.
-// exp(x) rounded once to float (through double). Kept out of line: the
-// whole-row passes of the select path call it from unrolled loops, where an
-// inlined copy per element made the kernel's code too large for the
-// instruction cache.
-#ifndef QS_EXP_NOINLINE
-#define QS_EXP_NOINLINE 1
-#endif
-#if QS_EXP_NOINLINE
-__device__ __noinline__
-#else
-__device__ __forceinline__
-#endif
-float exp_rounded(float x) {
-    return __double2float_rn(exp((double)x));
-}
-__device__ __forceinline__ uint32_t p_key(float sc, float M, float thr, float inv) {
-    if (!(sc >= thr)) return 0u;
-    const float e = exp_rounded(__fsub_rn(sc, M));
-    return min(__float_as_uint(__fmul_rn(e, inv)), 0x3F800000u);
 }
 
 __device__ float block_max_f(float v, Shared& s) {
@@ -1073,7 +1004,6 @@ __device__ __forceinline__ int reg_elem(int it, int tid, int j) {
 struct LdgSource {
     static constexpr bool kRegs = true;
     static constexpr bool kPick = false;  // penalized values are claimed at the row's end
-    static constexpr bool kSplit = false;
     float nxt[LDG_DEPTH][16];  // tiles it+1 .. it+LDG_DEPTH in flight
     __device__ __forceinline__ void begin(const Row& R) {
 #pragma unroll
@@ -1119,13 +1049,11 @@ __device__ __noinline__ bool ring_wait_slow(uint32_t bar, uint32_t par, int* abo
 
 // kPickable: stochastic rows with long histories pick their penalized values
 // up from the ring (a separate kernel instance, so the common case's code is
-// not affected by it). kSplit: a split launch (launch rows are column shards,
-// state_row), also an instance of its own.
-template <bool kPickable, bool kSplitRows>
+// not affected by it).
+template <bool kPickable>
 struct TmaSource {
     static constexpr bool kRegs = false;
     static constexpr bool kPick = kPickable;
-    static constexpr bool kSplit = kSplitRows;
     uint32_t ring_u32;  // NSTAGE tiles (shared-window address)
     uint32_t thr_off;   // 64 * tid + 16 * chunk_swz(tid)
     uint32_t full0, empty0;
@@ -1220,20 +1148,6 @@ __device__ __forceinline__ RowCtx row_ctx(const RowsArgs& a, int row, const quas
     return row_ctx_raw(a, row, pr, ring_len_raw(a, row), ring_head_raw(a, row), R);
 }
 
-// Split launches (a.split_B > 0): launch row `row` is column shard
-// row / split_B of state row row % split_B. state_row gives the index of the
-// row's parameters, PRNG word and ring; split_shard points c and R (set up
-// for the state row) at the shard's columns.
-template <bool kSplit>
-__device__ __forceinline__ int state_row(const RowsArgs& a, int row) {
-    if constexpr (kSplit) return row % a.split_B;
-    else return row;
-}
-__device__ __forceinline__ void split_shard(const RowsArgs& a, int row, int srow, RowCtx& c, Row& R) {
-    c.col0 = (int64_t)(row / a.split_B) * a.V;
-    R.ptr = a.logits + (int64_t)srow * a.ld + c.col0;
-}
-
 // row_ctx plus the penalty bitset of the row's history ids (consumer threads).
 // my_id: this thread's ring entry (threadIdx.x) when it is a column id, else
 // -1; its logit is copied into s.tfmax[threadIdx.x] (idle in kernel A) while
@@ -1246,11 +1160,9 @@ __device__ __forceinline__ bool ring_slot_used(const RowCtx& c, int p) {
 // Copies the inputs row_setup needs for `row` into shared memory (cp.async,
 // one group): parameters, ring length and head, ring slots 0..CONSUMERS-1
 // (raw positions, into tfmax). Rows past B are skipped.
-template <bool kSplit>
-__device__ __forceinline__ void stage_next_row(const RowsArgs& a, int lrow, SharedA& s) {
+__device__ __forceinline__ void stage_next_row(const RowsArgs& a, int row, SharedA& s) {
     const int tid = threadIdx.x;
-    if (lrow < a.B) {
-        const int row = state_row<kSplit>(a, lrow);
+    if (row < a.B) {
         if (a.d_params && tid < (int)(sizeof(quasar_sample_params) / 4))
             cp_async4(smem_u32(&s.nxt_pr) + 4u * tid, reinterpret_cast<const char*>(a.d_params + row) + 4 * tid);
         if (tid == 32 && has_len(a)) cp_async4(smem_u32(&s.nxt_len), a.hist_len + row);
@@ -1276,20 +1188,18 @@ __device__ __forceinline__ bool picks_in_stream(const RowCtx& c, const Row& R) {
 // row with a long history (more ring slots than consumer threads) picks its
 // penalized values up from the ring while it streams (pick_penalized) and
 // needs no staged logit.
-template <bool kPickTma, bool kSplit>
-__device__ __forceinline__ RowCtx row_setup(const RowsArgs& a, int lrow, Row& R, uint32_t* bits, SharedA& s,
+template <bool kPickTma>
+__device__ __forceinline__ RowCtx row_setup(const RowsArgs& a, int row, Row& R, uint32_t* bits, SharedA& s,
                                             int& my_id, bool staged) {
     const int tid = threadIdx.x;
     if (staged) {
         cp_async_wait_all();
         csync();  // every thread's copies have landed
     }
-    const int row = state_row<kSplit>(a, lrow);
     const quasar_sample_params pr = a.d_params ? (staged ? s.nxt_pr : a.d_params[row]) : a.h_params;
     const int len_raw = staged ? (has_len(a) ? s.nxt_len : a.hist_cap) : ring_len_raw(a, row);
     const int head_raw = staged ? (has_head(a) ? s.nxt_head : 0) : ring_head_raw(a, row);
-    RowCtx c = row_ctx_raw(a, row, pr, len_raw, head_raw, R);
-    if constexpr (kSplit) split_shard(a, lrow, row, c, R);
+    const RowCtx c = row_ctx_raw(a, row, pr, len_raw, head_raw, R);
     my_id = -1;
     if (R.use_pen) {
         for (int p = tid; p < c.cap; p += CONSUMERS) {
@@ -1531,7 +1441,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
     const uint8_t* bits8 = reinterpret_cast<const uint8_t*>(bits);
     Row R;
     int my_id;
-    const RowCtx c = row_setup<Src::kPick, Src::kSplit>(a, row, R, bits, s, my_id, staged);
+    const RowCtx c = row_setup<Src::kPick>(a, row, R, bits, s, my_id, staged);
     const bool pick = Src::kPick && picks_in_stream(c, R);
     const RowParams& P = c.P;
     src.begin(R);
@@ -1568,7 +1478,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
                 }
             });
         }
-        stage_next_row<Src::kSplit>(a, row + (int)gridDim.x, s);  // s.tfmax is free again
+        stage_next_row(a, row + (int)gridDim.x, s);  // s.tfmax is free again
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const float ov = __shfl_xor_sync(FULL, bv, o);
@@ -1746,7 +1656,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
             }
         });
     }
-    stage_next_row<Src::kSplit>(a, row + (int)gridDim.x, s);  // s.tfmax is free again
+    stage_next_row(a, row + (int)gridDim.x, s);  // s.tfmax is free again
     a.work_tfmax[(int64_t)row * CONSUMERS + tid] = m;
     {
         // anchor deficits, four per word (tbl_off), stored as whole words;
@@ -2234,7 +2144,7 @@ __global__ void __launch_bounds__(CONSUMERS, QS_A_CTAS) sample_rows_ldg(RowsArgs
     for (int row = blockIdx.x; row < a.B; row += gridDim.x) stream_row(a, row, src, bits, anc_s, s, row != (int)blockIdx.x);
 }
 
-template <bool kPickable, bool kSplit>
+template <bool kPickable>
 __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a) {
     extern __shared__ __align__(128) unsigned char dyn[];
     // the ring starts on a 64-byte boundary (the chunk swizzle flips address
@@ -2265,9 +2175,7 @@ __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a)
         const int64_t row_bytes = (int64_t)a.V * 4;
         uint32_t g = 0;
         for (int row = blockIdx.x; row < a.B; row += gridDim.x) {
-            const float* rp = kSplit ? a.logits + (int64_t)(row % a.split_B) * a.ld + (int64_t)(row / a.split_B) * a.V
-                                     : a.logits + (int64_t)row * a.ld;
-            const char* src = reinterpret_cast<const char*>(rp);
+            const char* src = reinterpret_cast<const char*>(a.logits + (int64_t)row * a.ld);
             for (int c = 0; c < ntiles; c++, g++) {
                 const int st = (int)(g % NSTAGE);
                 if (g >= (uint32_t)NSTAGE) {
@@ -2285,7 +2193,7 @@ __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a)
         }
         return;
     }
-    TmaSource<kPickable, kSplit> src;
+    TmaSource<kPickable> src;
     src.ring_u32 = smem_u32(ring);
     src.thr_off = 64u * threadIdx.x + 16u * chunk_swz(threadIdx.x);
     src.full0 = full0;
@@ -2373,18 +2281,13 @@ __global__ void __launch_bounds__(32 * SW_WARPS) sample_rows_shard_cand_warp(Row
     sm.thr = reinterpret_cast<uint16_t*>(base + (size_t)SW_CAP * 8);
     sm.bits = reinterpret_cast<uint32_t*>(base + (size_t)SW_CAP * 8 + CONSUMERS * 2);
     const int k = a.shard_k;
-    const bool split = a.split_B > 0;
-    const int nb = split ? a.split_B : a.B;  // rows per shard in all_stats
     // an aborted kernel A (bulk-copy ring timeout) left stale summaries: every
     // row sends the overflow mark, so the merge reports id -1
     const bool aborted = *reinterpret_cast<volatile int*>(a.work_abort) != 0;
     for (int row = blockIdx.x * SW_WARPS + w; row < a.B; row += gridDim.x * SW_WARPS) {
-        const int srow = split ? row % a.split_B : row;
-        const int rank = split ? row / a.split_B : a.shard_rank;
-        const quasar_sample_params pr = a.d_params ? a.d_params[srow] : a.h_params;
+        const quasar_sample_params pr = a.d_params ? a.d_params[row] : a.h_params;
         Row R;
-        RowCtx c = row_ctx(a, srow, pr, R);
-        if (split) split_shard(a, row, srow, c, R);
+        const RowCtx c = row_ctx(a, row, pr, R);
         const int64_t col0 = c.col0;
         const RowParams& P = c.P;
         uint64_t* out = a.shard_cand + (int64_t)row * k;
@@ -2396,7 +2299,7 @@ __global__ void __launch_bounds__(32 * SW_WARPS) sample_rows_shard_cand_warp(Row
         if (!(pr.temperature > 0.0f)) {
             // greedy: this shard's best column (kernel A), as in the CTA kernel
             if (lane == 0) {
-                const quasar_shard_stat st = a.all_stats[(int64_t)rank * nb + srow];
+                const quasar_shard_stat st = a.all_stats[(int64_t)a.shard_rank * a.B + row];
                 out[0] = st.best >= 0 ? ((uint64_t)ord_key(st.max) << 32) | (uint32_t)(~(uint32_t)(col0 + st.best))
                                       : 0ull;
             }
@@ -2415,7 +2318,7 @@ __global__ void __launch_bounds__(32 * SW_WARPS) sample_rows_shard_cand_warp(Row
         }
         const float4 info = a.work_info[row];
         const int npen = min(max(__float_as_int(info.z), 0), a.hist_cap);
-        shard_norm(a, srow, nb, R.M, R.inv);  // the row's global max and 1/sum
+        shard_norm(a, row, a.B, R.M, R.inv);  // the row's global max and 1/sum
         R.thr = __fsub_rn(R.M, 30.0f);
         const float* tf = a.work_tfmax + (int64_t)row * CONSUMERS;
         float lo = -INFINITY;
@@ -2788,8 +2691,8 @@ struct KernelCfg {
     std::atomic<size_t> smem_set[64];
     std::atomic<int> grid[64];  // resident CTAs of the kernel on each device
 };
-KernelCfg g_ldg, g_tma, g_tma_pick, g_tma_split, g_tma_pick_split, g_fin, g_fin_long, g_fin_shard,
-    g_fin_shard_long, g_merge, g_merge_warp, g_shard_warp;
+KernelCfg g_ldg, g_tma, g_tma_pick, g_fin, g_fin_long, g_fin_shard, g_fin_shard_long, g_merge, g_merge_warp,
+    g_shard_warp;
 std::mutex g_cfg_mu;
 
 cudaError_t configure(KernelCfg& cfg, const void* fn, int threads, size_t smem, int dev, int& grid) {
@@ -2850,14 +2753,10 @@ cudaError_t launch_stream(const RowsArgs& a, int dev, cudaStream_t stream) {
     if (a.tma) {
         const size_t smem = rows_tma_smem_bytes(a.V);
         int grid = 0;
-        // long histories: penalized values picked up in the stream; split
-        // launches: launch rows are column shards (an instance each)
-        const bool pick = a.hist && a.hist_cap > rows::CONSUMERS, split = a.split_B > 0;
-        const void* fn = split ? (pick ? (const void*)rows::sample_rows_tma<true, true>
-                                       : (const void*)rows::sample_rows_tma<false, true>)
-                               : (pick ? (const void*)rows::sample_rows_tma<true, false>
-                                       : (const void*)rows::sample_rows_tma<false, false>);
-        KernelCfg& cfg = split ? (pick ? g_tma_pick_split : g_tma_split) : (pick ? g_tma_pick : g_tma);
+        // long histories: penalized values picked up in the stream (an instance of its own)
+        const bool pick = a.hist && a.hist_cap > rows::CONSUMERS;
+        const void* fn = pick ? (const void*)rows::sample_rows_tma<true> : (const void*)rows::sample_rows_tma<false>;
+        KernelCfg& cfg = pick ? g_tma_pick : g_tma;
         err = configure(cfg, fn, rows::CONSUMERS + 32, smem, dev, grid);
         if (err != cudaSuccess) return err;
         void* args[] = {const_cast<RowsArgs*>(&a)};
@@ -2970,110 +2869,6 @@ cudaError_t launch_shard_merge(const RowsArgs& args, cudaStream_t stream) {
     if (err != cudaSuccess) return err;
     rows::sample_rows_merge<<<min(args.B, grid), rows::CONSUMERS, smem, stream>>>(args);
     return cudaGetLastError();
-}
-
-// ---------------------------------------------------------------------------
-// Split rows. With B rows the streaming kernel runs B CTAs (one per row), so
-// a small batch uses a few of the 148 SMs and its latency is one SM's
-// bandwidth over a whole row (~15 us for 608 KB). A small batch whose
-// parameters are on the host is instead streamed as G column shards per row
-// (G * B CTAs) by the streaming kernel's split instance, and finished by the
-// vocab-shard candidate kernel (one warp per shard row: the shard's top-k
-// keys against the row's global max and sum) and the shard merge kernel
-// (cuts and draw over the G * k keys, PRNG step, ring append) - the
-// three-phase vocab-sharded pick of one GPU, with the all-gathers done by
-// placement. Exact for greedy rows and for rows with 1 <= top_k <= 256 (every
-// kept element is among some shard's top_k); other rows stay on the one-CTA
-// path, where the candidate path's min-p bound or the exact select applies.
-#ifndef QS_SPLIT_MAX_G
-#define QS_SPLIT_MAX_G 8     // shards per row at most (16 and 32 were slower: the merge grows with G)
-#endif
-#ifndef QS_SPLIT_MAX_ROWS
-#define QS_SPLIT_MAX_ROWS 256  // shard rows (CTAs of the streaming kernel) per launch at most
-#endif
-#ifndef QS_SPLIT_MIN_COLS
-#define QS_SPLIT_MIN_COLS 2048  // columns per shard at least
-#endif
-// workspace of a split launch at most (long histories make the shard rows'
-// penalized lists large; such batches take the one-CTA path instead)
-constexpr size_t SPLIT_MAX_WS = (size_t)16 << 20;
-
-namespace {
-size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
-}  // namespace
-
-int split_shards(const RowsArgs& a) {
-    if (a.B < 1 || a.B > SPLIT_MAX_B || a.d_params || !a.tma) return 0;
-    if (a.flags & (QUASAR_FLAG_EXACT_SELECT | QUASAR_FLAG_NO_SPLIT)) return 0;
-    const quasar_sample_params& p = a.h_params;
-    if (p.temperature > 0.0f && !(p.top_k >= 1 && p.top_k <= SPLIT_MAX_K)) return 0;
-    // the workspace of the most shards B rows can get within SPLIT_MAX_WS (so
-    // a workspace of quasar_sampler_workspace_bytes covers any G chosen here)
-    if (split_workspace_bytes(a.B, 0, a.hist ? a.hist_cap : 0) == 0) return 0;
-    // the most shards whose columns stay a multiple of 4 (16-byte aligned
-    // bulk copies) and fit the one-warp candidate kernel
-    for (int G = QS_SPLIT_MAX_G; G >= 2; G >>= 1) {
-        const int vs = a.V / G;
-        if (a.V % G != 0 || vs % 4 != 0 || vs < QS_SPLIT_MIN_COLS || vs > rows::SW_MAX_COLS) continue;
-        if (G * a.B > QS_SPLIT_MAX_ROWS) continue;
-        return G;
-    }
-    return 0;
-}
-
-// [summaries of G*B shard rows (rows_workspace_bytes)][stats [G][B]][keys [G][B][k]].
-// G <= 0: the most shards a batch of B rows can be given (any V); 0 when that
-// exceeds SPLIT_MAX_WS (the batch is never split).
-size_t split_workspace_bytes(int B, int G, int hist_cap) {
-    if (B < 1 || B > SPLIT_MAX_B) return 0;
-    const bool largest = G <= 0;
-    if (largest)
-        for (G = QS_SPLIT_MAX_G; G > 2 && G * B > QS_SPLIT_MAX_ROWS; G >>= 1) {
-        }
-    const size_t R = (size_t)B * (size_t)G;
-    const size_t bytes = align256(rows_workspace_bytes((int)R, hist_cap)) +
-                         align256(R * sizeof(quasar_shard_stat)) + R * SPLIT_MAX_K * sizeof(uint64_t);
-    return largest && bytes > SPLIT_MAX_WS ? 0 : bytes;
-}
-
-cudaError_t launch_split_rows(const RowsArgs& args, int G, void* workspace, cudaStream_t stream) {
-    int dev = 0;
-    cudaError_t err = current_device(dev);
-    if (err != cudaSuccess) return err;
-    const int B = args.B, R = B * G, k = args.h_params.temperature > 0.0f ? args.h_params.top_k : 1;
-    char* ws = reinterpret_cast<char*>(workspace);
-    const size_t rows_bytes = align256(rows_workspace_bytes(R, args.hist ? args.hist_cap : 0));
-    quasar_shard_stat* stats = reinterpret_cast<quasar_shard_stat*>(ws + rows_bytes);
-    uint64_t* cand = reinterpret_cast<uint64_t*>(ws + rows_bytes + align256((size_t)R * sizeof(quasar_shard_stat)));
-    // phase 1: every shard row streamed once, its (max, sum, best) published
-    RowsArgs a = args;
-    a.B = R;
-    a.V = args.V / G;
-    a.split_B = B;
-    a.vec = args.vec && a.V % 8 == 0;  // shard starts 32-byte aligned
-    a.record = 0;
-    a.out = nullptr;
-    a.diag = nullptr;
-    layout_workspace(a, workspace);
-    a.shard_stats = stats;
-    err = launch_stream(a, dev, stream);
-    if (err != cudaSuccess) return err;
-    // phase 2: each shard row's top-k keys against the row's global max and sum
-    a.shard_stats = nullptr;
-    a.all_stats = stats;
-    a.shard_G = G;
-    a.shard_k = k;
-    a.shard_rank = 0;
-    a.shard_cand = cand;
-    err = launch_cand_warp(a, dev, stream);
-    if (err != cudaSuccess) return err;
-    // phase 3: the B rows' cuts, draws, PRNG steps and ring appends
-    RowsArgs m = args;
-    m.all_stats = stats;
-    m.shard_G = G;
-    m.shard_k = k;
-    m.shard_cand = cand;
-    return launch_shard_merge(m, stream);
 }
 
 }  // namespace qs

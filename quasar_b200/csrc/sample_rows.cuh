@@ -42,12 +42,6 @@ struct RowsArgs {
     const quasar_shard_stat* all_stats;    // [G][B] in (candidate and merge kernels)
     int shard_G, shard_k, shard_rank;
     uint64_t* shard_cand;                  // candidate kernel: [B][k] out; merge: [G][B][k] in
-    // split rows (a small batch spread over more CTAs, one GPU): > 0 in the
-    // streaming and candidate launches of launch_split_rows, where launch row
-    // r is column shard g = r / split_B of state row b = r % split_B (global
-    // columns [g*V, (g+1)*V) of logits row b); state (parameters, PRNG, ring)
-    // is indexed by b, summaries and shard outputs by r ([G][split_B] order)
-    int split_B;
 };
 
 size_t rows_smem_bytes(int V);      // one-CTA-per-row kernel
@@ -72,15 +66,13 @@ cudaError_t launch_shard_stats(const RowsArgs& args, void* workspace, cudaStream
 cudaError_t launch_shard_candidates(const RowsArgs& args, void* workspace, cudaStream_t stream);
 size_t rows_merge_smem_bytes(int G, int k);
 cudaError_t launch_shard_merge(const RowsArgs& args, cudaStream_t stream);
-// Split rows: a batch of at most SPLIT_MAX_B rows whose parameters are known
-// on the host (args.d_params NULL) is streamed as G column shards per row on
-// one GPU (G * B CTAs instead of B) and finished by the shard candidate and
-// merge kernels, when every row is greedy or has 1 <= top_k <= SPLIT_MAX_K.
-// split_shards returns G (0: the batch does not qualify).
+// Small batches (small_batch.cu): at most SPLIT_MAX_B rows whose parameters
+// are on the host (args.d_params NULL), each greedy or with 1 <= top_k <= 256,
+// are sampled by one fused kernel in which a cluster of G CTAs holds each row
+// in shared memory. small_batch_shards returns G (0: the batch does not
+// qualify); launch_small_batch needs no workspace.
 constexpr int SPLIT_MAX_B = 16;
-constexpr int SPLIT_MAX_K = 256;
-int split_shards(const RowsArgs& args);
-size_t split_workspace_bytes(int B, int G, int hist_cap);  // G <= 0: the largest G any V can get (0: no split)
-cudaError_t launch_split_rows(const RowsArgs& args, int G, void* workspace, cudaStream_t stream);
+int small_batch_shards(const RowsArgs& args);
+cudaError_t launch_small_batch(const RowsArgs& args, int G, cudaStream_t stream);
 
 }  // namespace qs

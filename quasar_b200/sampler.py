@@ -143,7 +143,8 @@ def pick_batch(logits, rng, *, params=None, d_params=None, hist=None, hist_len=N
 
 def split_shards(B: int, V: int, *, params=None, per_row_params: bool = False, hist_cap: int = 0, flags: int = 0,
                  ld: int = None, ptr: int = 256) -> int:
-    """Column shards per row that pick_batch streams a batch of B rows in (0: one CTA per row).
+    """CTAs per row (cluster size) of the fused small-batch kernel pick_batch uses for
+    a batch of B rows (0: the streaming and finishing kernels, one CTA per row).
 
     params: the record shared by all rows (as pick_batch's ``params``);
     per_row_params: the rows have device parameters instead (never split).

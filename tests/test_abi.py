@@ -107,15 +107,15 @@ def test_params_layout_matches_oracle():
     assert q.PARAMS_DTYPE == O.PARAMS_DTYPE
 
 
-def test_split_decision_and_workspace_without_gpu():
-    """Which batches pick_batch streams as column shards (host arithmetic:
-    small batches with host parameters, greedy or 1 <= top_k <= 256, rows
-    that the bulk-copy ring can stream, a shard width that is a multiple of
-    4), and that quasar_sampler_workspace_bytes covers the split."""
+def test_small_batch_decision_without_gpu():
+    """Which batches pick_batch samples with the fused cluster kernel (host
+    arithmetic: at most 16 rows with host parameters, greedy or
+    1 <= top_k <= 256, rows the bulk-copy ring can stream, V % 32 == 0 and
+    V >= 8192), and that the workspace query is the one-CTA path's."""
     import quasar_b200 as q
     V = 151936
     cfg1 = dict(temperature=0.7, top_k=20, top_p=0.8, repeat_penalty=1.1)
-    assert [q.split_shards(B, V, params=cfg1, hist_cap=64) for B in (1, 2, 8, 9, 16, 17)] == [8, 8, 8, 8, 8, 0]
+    assert [q.split_shards(B, V, params=cfg1, hist_cap=64) for B in (1, 2, 8, 16, 17)] == [8, 8, 8, 8, 0]
     assert q.split_shards(1, V, params=dict(temperature=0.0)) == 8              # greedy
     assert q.split_shards(1, V, params=dict(temperature=1.0, top_k=256)) == 8
     assert q.split_shards(1, V, params=dict(temperature=1.0, top_k=257)) == 0   # beyond a shard's keys
@@ -129,14 +129,8 @@ def test_split_decision_and_workspace_without_gpu():
     assert q.split_shards(1, V, params=cfg1, ld=V + 2) == 0                     # ld % 4 != 0
     assert q.split_shards(1, V, params=cfg1, ld=V + 4) == 8
     assert q.split_shards(1, 20000, params=cfg1) == 8                           # 8 x 2500
-    assert q.split_shards(1, 20004, params=cfg1) == 0                           # no width % 4 == 0 >= 2048
-    assert q.split_shards(1, 4000, params=cfg1) == 0                            # shards under 2048 columns
-    assert q.split_shards(1, V, params=cfg1, hist_cap=2048) == 8
-    assert q.split_shards(16, V, params=cfg1, hist_cap=100000) == 0             # split workspace over 16 MiB
-    for B, H in ((1, 0), (1, 64), (4, 256), (16, 2048), (17, 64), (16, 100000), (512, 256)):
-        rows = 256 + B * (16 + 4 * 256 + 8 * H + 40 * 256 + 8 * 256)           # one CTA per row
-        assert q.workspace_bytes(B, H) >= rows
-    assert q.workspace_bytes(17, 64) == 256 + 17 * (16 + 1024 + 512 + 10240 + 2048)
-    assert q.workspace_bytes(16, 100000) == 256 + 16 * (16 + 1024 + 800000 + 10240 + 2048)
-    assert q.workspace_bytes(1, 64) > 8 * (1024 + 10240)                           # the 8 shard rows' summaries
-    assert q.workspace_bytes(512, 256) <= q.QUASAR_NOALLOC_WORKSPACE_BYTES
+    assert q.split_shards(1, 20004, params=cfg1) == 0                           # 20004 / 8 not whole
+    assert q.split_shards(1, 4000, params=cfg1) == 0                            # shards under 1024 columns
+    assert q.split_shards(16, V, params=cfg1, hist_cap=100000) == 8             # no workspace involved
+    for B, H in ((1, 0), (1, 64), (4, 256), (17, 64), (16, 100000)):
+        assert q.workspace_bytes(B, H) == 256 + B * (16 + 4 * 256 + 8 * H + 40 * 256 + 8 * 256)

@@ -1,6 +1,6 @@
-"""Split rows: small batches with host parameters, each row streamed as G
-column shards by G CTAs and finished by the shard candidate and merge
-kernels (quasar_sampler_split_shards > 0), against the reference
+"""Small batches: rows with host parameters sampled by the fused cluster
+kernel (a cluster of G CTAs per row, each holding V/G columns in shared
+memory; quasar_sampler_split_shards > 0), against the reference
 (oracle/_ref: sample.c compiled unmodified, sample.c:111-178) and against
 the same calls on one CTA per row (QUASAR_FLAG_NO_SPLIT).
 
@@ -110,10 +110,10 @@ def test_split_wide_top_k_with_top_p_and_min_p():
 
 
 def test_split_tied_logits():
-    """Logits quantised to 7 values: every per-thread maximum ties, so each
-    shard's bound lets ~2700 elements through (more than the one-warp
-    candidate kernel holds) and the shards take their exact top k by a radix
-    select; ties go to the lowest ids, as the reference's sort leaves them."""
+    """Logits quantised to 7 values: each shard of 18,992 columns holds ~2,700
+    elements tied at the row maximum, more than a CTA lists, so the CTAs take
+    their exact top k by a radix select over (p, id) keys; ties go to the
+    lowest ids, as the reference's sort leaves them."""
     import torch
     B = 4
     base = torch.randint(-3, 4, (B, V_FULL), generator=torch.Generator().manual_seed(0)).float()
@@ -128,8 +128,8 @@ def test_split_tied_logits():
 
 
 def test_split_long_history_rings():
-    """Rings of 512 slots (the streaming kernel's split instance that picks
-    penalized values up from its ring), partly filled, strong penalty."""
+    """Rings of 512 slots, partly filled, strong penalty (penalized columns
+    in every shard)."""
     import torch
     B, H = 3, 512
     logits, hist = gpu_inputs(O.SYNTH_ZIPF, 5, B, V_FULL, 1.1, H=H, hist_seed=6)
@@ -163,10 +163,10 @@ def test_split_uneven_vocab_and_unsplit_shapes():
         assert q.split_shards(B, V, params=prm, hist_cap=32, flags=q.FLAG_NO_SPLIT) == 0
 
 
-def test_split_caller_workspace_sizes():
-    """A caller workspace of quasar_sampler_workspace_bytes splits; one of the
-    one-CTA size only (rows_workspace_bytes) takes the one-CTA path; both
-    match the reference and each other."""
+def test_small_batch_ignores_workspace_and_no_alloc_entry():
+    """The fused kernel uses no workspace: a caller workspace of the one-CTA
+    size, the library's own and the no-allocation entry give the same
+    results, all matching the reference."""
     import torch
     import quasar_b200 as q
     B, H = 2, 64
@@ -174,16 +174,31 @@ def test_split_caller_workspace_sizes():
     logits, hist = gpu_inputs(O.SYNTH_NORMAL, 99, B, V_FULL, 3.0, H=H, hist_seed=98)
     seeds = _seeds(B, 9900)
     res, rng_ref = run_oracle(logits, prm, seeds, hist=hist)
+    nbytes = q.workspace_bytes(B, H)
+    ws = torch.empty(nbytes + 256, dtype=torch.uint8, device="cuda")
+    ws = ws[(-ws.data_ptr()) % 256:][:nbytes]
     outs = []
-    # 64 KB holds the one-CTA summaries of 2 rows (~28 KB), not the 64 shard rows
-    for nbytes in (q.workspace_bytes(B, H), 64 * 1024):
-        ws = torch.empty(nbytes + 256, dtype=torch.uint8, device="cuda")
-        ws = ws[(-ws.data_ptr()) % 256:][:nbytes]
+    for mode in ("caller", "library", "noalloc"):
         rng = torch.from_numpy(seeds.view(np.int64).copy()).cuda()
         diag = torch.zeros(B, 4, dtype=torch.int32, device="cuda")
-        out = q.pick_batch(logits, rng, params=prm[:1], hist=hist, diag=diag, workspace=ws)
+        out = torch.empty(B, dtype=torch.int32, device="cuda")
+        if mode == "noalloc":
+            hp = q.SampleParams(*(float(prm[0][f]) for f in ("temperature", "top_p", "min_p", "repeat_penalty")),
+                                int(prm[0]["top_k"]), 0)
+            import ctypes
+            rc = q.lib().quasar_sampler_pick_batch_noalloc(
+                ctypes.c_void_p(logits.data_ptr()), V_FULL, B, V_FULL, None, ctypes.byref(hp),
+                ctypes.c_void_p(rng.data_ptr()), ctypes.c_void_p(hist.data_ptr()), H, None, None, 0,
+                ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(diag.data_ptr()), 0,
+                ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+            assert rc == 0
+        else:
+            q.pick_batch(logits, rng, params=prm[:1], hist=hist, diag=diag, out=out,
+                         workspace=ws if mode == "caller" else None)
         torch.cuda.synchronize()
         got = (out.cpu().numpy(), diag.cpu().numpy().view(q.DIAG_DTYPE).reshape(B), rng.cpu().numpy().view(np.uint64))
         assert_parity(*got, res, rng_ref, max_mismatch_frac=0.5)
         outs.append(got)
-    _same_as_unsplit(outs[0], outs[1], res)
+    for o in outs[1:]:
+        assert np.array_equal(o[0], outs[0][0]) and np.array_equal(o[2], outs[0][2])
+        assert np.array_equal(o[1]["p_chosen"].view(np.uint32), outs[0][1]["p_chosen"].view(np.uint32))
