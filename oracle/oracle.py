@@ -35,9 +35,20 @@ assert PARAMS_DTYPE.itemsize == 24 and RESULT_DTYPE.itemsize == 40
 _libs: dict[str, ctypes.CDLL] = {}
 
 
+def reference_tree() -> str | None:
+    """The franzvill/quasar checkout to build the reference from: the one
+    QUASAR_REFERENCE names, else a checkout named ``reference`` beside this
+    repository; None when neither holds sample.c."""
+    for d in (os.environ.get("QUASAR_REFERENCE"), os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")):
+        if d and os.path.isfile(os.path.join(d, "sample.c")):
+            return d
+    return None
+
+
 def build() -> None:
     """Compile oracle/ (restatement always; reference build when its tree exists)."""
-    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    ref = reference_tree()
+    subprocess.run(["make", "-s", "-C", HERE] + ([f"REF={ref}"] if ref else []), check=True)
 
 
 def available(backend: str) -> bool:
