@@ -60,8 +60,7 @@ struct Smem {
     int abort;
     uint32_t hist[256]; // radix-select bins
     uint32_t pick_bin, pick_above;
-    float tmax[T];      // each thread's max over its columns of the shard
-    float floor_k;      // the k-th largest of tmax
+    float wk[NW];       // each warp's ceil(k/8)-th largest thread max
     uint64_t rng;       // the row's PRNG word (CTA 0)
 };
 
@@ -213,7 +212,25 @@ __global__ void __launch_bounds__(T) sample_rows_small(RowsArgs a, int G) {
             d4[q] = make_float4(x[0], x[1], x[2], x[3]);
         }
     }
-    s.tmax[tid] = m;  // (stochastic rows: a bound for the shard's top k)
+    const int k = greedy ? 1 : min(max(P.top_k, 1), KMAX);
+    if (!greedy) {
+        // A bound for the shard's top k: each warp sorts its 32 thread maxima
+        // (a shuffle bitonic network, descending) and keeps its c-th largest,
+        // c = ceil(k/8); the smallest of the 8 has at least 8c >= k thread
+        // maxima - k distinct elements - at or above it, so it is at most the
+        // shard's k-th largest value.
+        float v = m;
+#pragma unroll
+        for (int size = 2; size <= 32; size <<= 1)
+#pragma unroll
+            for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                const float o = __shfl_xor_sync(FULL, v, stride);
+                const bool desc = (lane & size) == 0;  // this segment's direction
+                v = (((lane & stride) == 0) == desc) ? fmaxf(v, o) : fminf(v, o);
+            }
+        const float vc = __shfl_sync(FULL, v, (k + NW - 1) / NW - 1);
+        if (lane == 0) s.wk[warp] = vc;
+    }
     // block max (greedy: value desc, column asc)
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -237,38 +254,12 @@ __global__ void __launch_bounds__(T) sample_rows_small(RowsArgs a, int G) {
             mi = s.ri[w];
         }
     double S = 0.0;
-    const int k = greedy ? 1 : min(max(P.top_k, 1), KMAX);
-    if (!greedy && warp == 0) {
-        // The k-th largest thread max bounds the shard's k-th largest value
-        // from below (the k largest thread maxima are k elements at or above
-        // it): warp 0 finds it by a radix select over the order-preserving
-        // keys, 8 per lane, bit by bit, while warps 1-7 sum
-        uint32_t key8[T / 32];
-#pragma unroll
-        for (int q = 0; q < T / 32; q++) key8[q] = ord_key(s.tmax[q * 32 + lane]);
-        uint32_t prefix = 0u;
-        int need = k;  // rank (1-based) of the wanted key among those matching prefix
-#pragma unroll 1
-        for (int bb = 31; bb >= 0; bb--) {
-            const uint32_t want = (prefix << 1) | 1u;  // the bit-bb-set half sorts first
-            int c = 0;
-#pragma unroll
-            for (int q = 0; q < T / 32; q++) c += ((key8[q] >> bb) == want) ? 1 : 0;
-            c = __reduce_add_sync(FULL, c);
-            if (c >= need) {
-                prefix = want;
-            } else {
-                prefix = want - 1u;
-                need -= c;
-            }
-        }
-        if (lane == 0) s.floor_k = ord_key_inv(prefix);
-    } else if (!greedy && m > -INFINITY) {
-        // sum of exp(v - m) by warps 1-7, fp32 over 16 terms at a time, double across
+    if (!greedy && m > -INFINITY) {
+        // sum of exp(v - m), fp32 over 16 terms at a time, double across
         float part = 0.0f;
         int n4 = 0;
 #pragma unroll 2
-        for (int q = tid - 32; q < Vs4; q += T - 32) {
+        for (int q = tid; q < Vs4; q += T) {
             const float4 v4 = d4[q];
             part += (exp_fast(__fsub_rn(v4.x, m)) + exp_fast(__fsub_rn(v4.y, m))) +
                     (exp_fast(__fsub_rn(v4.z, m)) + exp_fast(__fsub_rn(v4.w, m)));
@@ -336,10 +327,12 @@ __global__ void __launch_bounds__(T) sample_rows_small(RowsArgs a, int G) {
         const float thr = __fsub_rn(M, 30.0f);
         float lo0 = thr;
         if (P.min_p > 0.0f) lo0 = fmaxf(lo0, __fadd_rn(M, logf(fminf(P.min_p, 1.0f)) - 0.01f));
-        // Only elements at or above the k-th largest thread max (s.floor_k)
-        // are listed, less a tie margin that keeps every element whose p
-        // could equal the k-th one's.
-        const float fk = s.floor_k;
+        // Only elements at or above the warps' bound (s.wk) are listed, less a
+        // tie margin that keeps every element whose p could equal the k-th
+        // one's; as raw (value, column) entries, their keys computed below.
+        float fk = s.wk[0];
+#pragma unroll
+        for (int w = 1; w < NW; w++) fk = fminf(fk, s.wk[w]);
         const float lo = fk > -INFINITY ? fmaxf(lo0, fk - (1e-5f + 1e-5f * fabsf(fk))) : lo0;
 #pragma unroll 2
         for (int q = tid; q < Vs4; q += T) {
@@ -349,13 +342,20 @@ __global__ void __launch_bounds__(T) sample_rows_small(RowsArgs a, int G) {
             for (int j = 0; j < 4; j++)
                 if (x[j] >= lo) {
                     const int pos = atomicAdd(&s.nlist, 1);
-                    if (pos < LCAP)
-                        list[pos] = ((uint64_t)p_key(x[j], M, thr, inv) << 32) |
-                                    (uint32_t)(~(uint32_t)(col0 + 4 * q + j));
+                    if (pos < LCAP) list[pos] = ((uint64_t)__float_as_uint(x[j]) << 32) | (uint32_t)(4 * q + j);
                 }
         }
         bsync();
         int nl = s.nlist;
+        if (nl <= LCAP) {
+            // the listed entries' keys (p desc, global id asc), one per thread
+            for (int i = tid; i < nl; i += T) {
+                const uint64_t en = list[i];
+                list[i] = ((uint64_t)p_key(__uint_as_float((uint32_t)(en >> 32)), M, thr, inv) << 32) |
+                          (uint32_t)(~(uint32_t)(col0 + (uint32_t)en));
+            }
+            bsync();
+        }
         if (nl > LCAP) {
             // more elements tie at the k-th value than the list holds: the
             // exact k-th key (p desc, id asc) over them, then exactly k keys
@@ -416,18 +416,24 @@ __global__ void __launch_bounds__(T) sample_rows_small(RowsArgs a, int G) {
         for (int i = tid; i < n; i += T) {
             const uint64_t key = keys[i];
             if ((key >> 32) == 0ull) continue;
-            const int gi = i / k;
-            int rank = i - gi * k;
-            for (int h = 0; h < G; h++) {
-                if (h == gi) continue;
-                const uint64_t* lst = keys + h * k;
-                int l0 = 0, l1 = k;  // first position whose key is not greater
-                while (l0 < l1) {
-                    const int mid = (l0 + l1) >> 1;
-                    if (lst[mid] > key) l0 = mid + 1;
-                    else l1 = mid;
+            int rank = 0;
+            if (n <= 512) {
+                // every key against every key, all threads reading the same one
+                for (int j = 0; j < n; j++) rank += keys[j] > key ? 1 : 0;
+            } else {
+                const int gi = i / k;
+                rank = i - gi * k;  // its place in its own list, plus per other list
+                for (int h = 0; h < G; h++) {
+                    if (h == gi) continue;
+                    const uint64_t* lst = keys + h * k;
+                    int l0 = 0, l1 = k;  // first position whose key is not greater
+                    while (l0 < l1) {
+                        const int mid = (l0 + l1) >> 1;
+                        if (lst[mid] > key) l0 = mid + 1;
+                        else l1 = mid;
+                    }
+                    rank += l0;
                 }
-                rank += l0;
             }
             if (rank < L) sorted[rank] = key;
         }
