@@ -1324,16 +1324,17 @@ __device__ __forceinline__ void mask_penalized(const Row& R, const uint8_t* bits
 // mask_penalized plus the pick-up of the penalized values (sample.c:118-128)
 // from the ring chunk the tile came from (`stage`: this thread's 64 bytes,
 // chunk k of register chunk k at stage ^ 16k, see TmaSource::get): each
-// penalized element is penalized exactly (IEEE divide / multiply), scaled,
-// joins the thread's running max m and sum S (against m_ref, as the streamed
-// terms do) and is listed with its scaled value for kernel B. The thread's
-// 16 bitset bits are cleared once read, so the bitset is all zero at the
-// row's end. Every column is streamed once, so every distinct history id is
-// picked up once.
+// penalized element's raw logit is listed with its column; the list is
+// penalized, scaled and summed at the row's end by every thread together
+// (finish_picked), not here, where only the lanes holding a penalized element
+// would do the work (about 7 of 32 at 2048 history ids: the arithmetic in
+// this loop cost 0.9 ms of a 2.7 ms config-5 call). The thread's 16 bitset
+// bits are cleared once read, so the bitset is all zero at the row's end.
+// Every column is streamed once, so every distinct history id is picked up
+// once.
 template <bool kCheck>
 __device__ __forceinline__ void pick_penalized(const Row& R, uint8_t* bits8, const float4* lut, float* v, int it,
-                                               uint32_t stage, int2* pen, int* npen, float& m, float& m_ref,
-                                               double& S) {
+                                               uint32_t stage, int2* pen, int* npen) {
     const int o0 = it * OCT_TILE + 2 * (int)threadIdx.x;
     const uint32_t mb = (!kCheck || o0 < R.noct) ? *reinterpret_cast<const uint16_t*>(bits8 + o0) : 0u;
     if (__any_sync(FULL, mb != 0u)) {
@@ -1360,15 +1361,7 @@ __device__ __forceinline__ void pick_penalized(const Row& R, uint8_t* bits8, con
                 b &= b - 1u;
                 float x;
                 asm volatile("ld.shared.f32 %0, [%1];" : "=f"(x) : "r"((stage ^ (16u * (uint32_t)(j >> 2))) + 4u * (uint32_t)(j & 3)));
-                const float sc = __fmul_rn(penalize(x, R.rp), R.inv_t);
-                pen[pos++] = make_int2(reg_elem(it, (int)threadIdx.x, j), __float_as_int(sc));
-                m = fmaxf(m, sc);
-                if (sc > m_ref + REF_SLACK) {
-                    S = S * exp((double)m_ref - (double)sc) + 1.0;
-                    m_ref = sc;
-                } else if (sc > -INFINITY) {
-                    S += (double)exp_fast(__fsub_rn(sc, m_ref));  // like the streamed terms
-                }
+                pen[pos++] = make_int2(reg_elem(it, (int)threadIdx.x, j), __float_as_int(x));  // raw logit
             } while (b);
         }
     }
@@ -1549,7 +1542,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
             if constexpr (kPen) mask_penalized<kMaybeLast>(R, bits8, s.pen_lut, v, it);
             if constexpr (kPick) {
                 pick_penalized<kMaybeLast>(R, reinterpret_cast<uint8_t*>(bits), s.pen_lut, v, it, src.stage_addr(),
-                                           a.work_pen + (int64_t)row * a.hist_cap, &s.npen, m, m_ref, S);
+                                           a.work_pen + (int64_t)row * a.hist_cap, &s.npen);
                 src.release();
             }
             // sample.c:142: sc = l * inv_t, rounded exactly like the reference
@@ -1638,6 +1631,26 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
         if (pick) run(std::false_type(), P2());
         else if (R.use_pen) run(std::false_type(), P1());
         else run(std::false_type(), P0());
+    }
+    if (pick) {
+        csync();  // the picked list is complete
+        // its raw logits penalized exactly (IEEE divide / multiply) and
+        // scaled, joining the running max and sum (against m_ref, as the
+        // streamed terms do); the list keeps the scaled values for kernel B
+        int2* pen = a.work_pen + (int64_t)row * a.hist_cap;
+        const int np = min(s.npen, a.hist_cap);
+        for (int i = tid; i < np; i += CONSUMERS) {
+            const int2 e = pen[i];
+            const float sc = __fmul_rn(penalize(__int_as_float(e.y), R.rp), R.inv_t);
+            pen[i].y = __float_as_int(sc);
+            m = fmaxf(m, sc);
+            if (sc > m_ref + REF_SLACK) {
+                S = S * exp((double)m_ref - (double)sc) + 1.0;
+                m_ref = sc;
+            } else if (sc > -INFINITY) {
+                S += (double)exp_fast(__fsub_rn(sc, m_ref));  // like the streamed terms
+            }
+        }
     }
     if (R.use_pen && !pick) {
         csync();
