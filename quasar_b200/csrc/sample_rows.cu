@@ -140,7 +140,6 @@ struct Shared {
 
 // Kernel A's shared state: the common slots plus the penalty mask table.
 struct SharedA : Shared {
-    float4 pen_lut[16];   // nibble n -> +0 / -inf per bit (penalized elements leave the stream)
     // the CTA's next row, copied during the current row's tail (stage_next_row):
     // parameters and ring position; its first CONSUMERS ring slots go to tfmax
     quasar_sample_params nxt_pr;
@@ -1298,26 +1297,21 @@ __device__ __forceinline__ void stream_tiles(const Row& R, Src& src, Shared& s, 
     }
 }
 
-// Streaming form of exclude_penalized: the octets' bitset nibbles index a
-// 16-entry table of float4 {0 or -inf} that is added to the values (x + 0 =
-// x, x + -inf = -inf for finite x), with no per-element branch; warps with no
-// penalized element in the tile skip it.
+// Streaming form of exclude_penalized: the thread's 16 bitset bits select
+// -inf for its penalized elements (one select per element; a 16-entry table
+// of float4 {0, -inf} added per nibble cost four 16-byte shared loads per
+// thread and was slower: config 3 0.526 -> 0.521 ms, config 5 2.54 -> 2.52
+// ms); warps with no penalized element in the tile skip it.
 // kCheck = false: tile it is not the row's last, so its octets are in range
 template <bool kCheck = true>
-__device__ __forceinline__ void mask_penalized(const Row& R, const uint8_t* bits8, const float4* lut, float* v,
-                                               int it) {
+__device__ __forceinline__ void mask_penalized(const Row& R, const uint8_t* bits8, float* v, int it) {
     // the thread's 16 bits (pen_bit order = register order), one 16-bit load
     const int o0 = it * OCT_TILE + 2 * (int)threadIdx.x;
     const uint32_t m = (!kCheck || o0 < R.noct) ? *reinterpret_cast<const uint16_t*>(bits8 + o0) : 0u;
     if (__any_sync(FULL, m != 0u)) {
-        const float4 q[4] = {lut[m & 15u], lut[(m >> 4) & 15u], lut[(m >> 8) & 15u], lut[m >> 12]};
 #pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const f32x2 lo = add2(pack2(v[4 * k], v[4 * k + 1]), pack2(q[k].x, q[k].y));
-            const f32x2 hi = add2(pack2(v[4 * k + 2], v[4 * k + 3]), pack2(q[k].z, q[k].w));
-            unpack2(lo, v[4 * k], v[4 * k + 1]);
-            unpack2(hi, v[4 * k + 2], v[4 * k + 3]);
-        }
+        for (int j = 0; j < 16; j++)
+            if ((m >> j) & 1u) v[j] = -INFINITY;
     }
 }
 
@@ -1333,19 +1327,16 @@ __device__ __forceinline__ void mask_penalized(const Row& R, const uint8_t* bits
 // Every column is streamed once, so every distinct history id is picked up
 // once.
 template <bool kCheck>
-__device__ __forceinline__ void pick_penalized(const Row& R, uint8_t* bits8, const float4* lut, float* v, int it,
-                                               uint32_t stage, int2* pen, int* npen) {
+__device__ __forceinline__ void pick_penalized(const Row& R, uint8_t* bits8, float* v, int it, uint32_t stage,
+                                               int2* pen, int* npen) {
     const int o0 = it * OCT_TILE + 2 * (int)threadIdx.x;
     const uint32_t mb = (!kCheck || o0 < R.noct) ? *reinterpret_cast<const uint16_t*>(bits8 + o0) : 0u;
     if (__any_sync(FULL, mb != 0u)) {
-        const float4 q[4] = {lut[mb & 15u], lut[(mb >> 4) & 15u], lut[(mb >> 8) & 15u], lut[mb >> 12]};
+        // a select per element, as mask_penalized (with 2048 history ids
+        // nearly every warp takes this branch on every tile)
 #pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const f32x2 lo = add2(pack2(v[4 * k], v[4 * k + 1]), pack2(q[k].x, q[k].y));
-            const f32x2 hi = add2(pack2(v[4 * k + 2], v[4 * k + 3]), pack2(q[k].z, q[k].w));
-            unpack2(lo, v[4 * k], v[4 * k + 1]);
-            unpack2(hi, v[4 * k + 2], v[4 * k + 3]);
-        }
+        for (int j = 0; j < 16; j++)
+            if ((mb >> j) & 1u) v[j] = -INFINITY;
         // list positions: one shared atomic per warp for all of its picks
         // (the whole warp is here: the branch condition is warp-uniform)
         const int cnt = __popc(mb);
@@ -1364,14 +1355,6 @@ __device__ __forceinline__ void pick_penalized(const Row& R, uint8_t* bits8, con
                 pen[pos++] = make_int2(reg_elem(it, (int)threadIdx.x, j), __float_as_int(x));  // raw logit
             } while (b);
         }
-    }
-}
-
-__device__ __forceinline__ void init_pen_lut(SharedA& s) {
-    if (threadIdx.x < 16) {
-        const int n = threadIdx.x;
-        s.pen_lut[n] = make_float4((n & 1) ? -INFINITY : 0.0f, (n & 2) ? -INFINITY : 0.0f,
-                                   (n & 4) ? -INFINITY : 0.0f, (n & 8) ? -INFINITY : 0.0f);
     }
 }
 
@@ -1446,7 +1429,7 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
         for (int it = 0; it < R.ntiles; it++) {
             float v[16];
             src.get(R, it, v, s);
-            if (R.use_pen) mask_penalized(R, bits8, s.pen_lut, v, it);
+            if (R.use_pen) mask_penalized(R, bits8, v, it);
             src.release();
             float mt = v[0];
 #pragma unroll
@@ -1539,9 +1522,9 @@ __device__ __forceinline__ void stream_row(const RowsArgs& a, int row, Src& src,
         constexpr bool kPick = decltype(pen)::value == 2;
         auto body = [&](float (&v)[16], int it, auto last) {
             constexpr bool kMaybeLast = decltype(last)::value;
-            if constexpr (kPen) mask_penalized<kMaybeLast>(R, bits8, s.pen_lut, v, it);
+            if constexpr (kPen) mask_penalized<kMaybeLast>(R, bits8, v, it);
             if constexpr (kPick) {
-                pick_penalized<kMaybeLast>(R, reinterpret_cast<uint8_t*>(bits), s.pen_lut, v, it, src.stage_addr(),
+                pick_penalized<kMaybeLast>(R, reinterpret_cast<uint8_t*>(bits), v, it, src.stage_addr(),
                                            a.work_pen + (int64_t)row * a.hist_cap, &s.npen);
                 src.release();
             }
@@ -2151,7 +2134,6 @@ __global__ void __launch_bounds__(CONSUMERS, QS_A_CTAS) sample_rows_ldg(RowsArgs
     __shared__ float anc_s[NCK * CONSUMERS];
     for (int i = threadIdx.x; i < a.nwords; i += CONSUMERS) bits[i] = 0u;
     if (threadIdx.x == 0) s.abort = 0;
-    init_pen_lut(s);
     csync();
     LdgSource src;
     for (int row = blockIdx.x; row < a.B; row += gridDim.x) stream_row(a, row, src, bits, anc_s, s, row != (int)blockIdx.x);
@@ -2178,7 +2160,6 @@ __global__ void __launch_bounds__(CONSUMERS + 32, 3) sample_rows_tma(RowsArgs a)
         s.abort = 0;
     }
     for (int i = threadIdx.x; i < a.nwords; i += blockDim.x) bits[i] = 0u;
-    init_pen_lut(s);
     __syncthreads();
 
     if (threadIdx.x >= CONSUMERS) {
