@@ -210,7 +210,7 @@ def run_reference_arm(args) -> None:
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": workload_config(args.gpus),
             "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": kind,
-                             "sample": f"{sample} config-3 rows per step (rows [k*{sample}, "
+                             "sample": f"{sample} {CFG['text'].split(':')[0]} rows per step (rows [k*{sample}, "
                                        f"(k+1)*{sample}) of the workload), one sampler object "
                                        f"per row, {threads} pthreads"},
             "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0,
@@ -368,7 +368,7 @@ def run_ours(args) -> None:
         rows = max(64, min(1024, 32 * threads))
         rate, kind, dt = time_cpu_reference(rows, threads)
         line["cpu_baseline"] = {"value": rate, "unit": "rows/s", "cores": threads, "kind": kind,
-                                "sample": f"first {rows} rows of the config-3 workload "
+                                "sample": f"first {rows} rows of the {CFG['text'].split(':')[0]} workload "
                                           f"({dt:.1f} s wall on {threads} threads)"}
     if rank == 0:
         print(json.dumps(line), flush=True)
